@@ -1,0 +1,97 @@
+"""ctypes binding of libtcx.so (the C ABI declared in include/tcx.h).
+
+The library is built in-tree (tensorcast_b200/_lib/libtcx.so). There is no CPU
+fallback: if the library is missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from .build import LIB_PATH, build_native
+
+_lock = threading.Lock()
+_lib = None
+
+OK = 0
+INVALID_ARGUMENT = 3
+DEADLINE_EXCEEDED = 4
+NOT_FOUND = 5
+RESOURCE_EXHAUSTED = 8
+FAILED_PRECONDITION = 9
+UNIMPLEMENTED = 12
+INTERNAL = 13
+DATA_LOSS = 15
+
+_CODE_NAMES = {0: "OK", 1: "CANCELLED", 2: "UNKNOWN", 3: "INVALID_ARGUMENT", 4: "DEADLINE_EXCEEDED",
+               5: "NOT_FOUND", 8: "RESOURCE_EXHAUSTED", 9: "FAILED_PRECONDITION", 11: "OUT_OF_RANGE",
+               12: "UNIMPLEMENTED", 13: "INTERNAL", 14: "UNAVAILABLE", 15: "DATA_LOSS"}
+
+
+class TcxError(RuntimeError):
+    """A libtcx call failed; ``code`` is the absl status code number."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{_CODE_NAMES.get(code, code)}: {message}")
+        self.code = code
+        self.message = message
+
+
+class TcxInvalidArgument(TcxError, ValueError):
+    pass
+
+
+def _raise(code: int) -> None:
+    msg = _lib.tcx_last_error().decode("utf-8", "replace")
+    if code == INVALID_ARGUMENT:
+        raise TcxInvalidArgument(code, msg)
+    raise TcxError(code, msg)
+
+
+# Every function exported by include/tcx.h with (restype, argtypes).
+_c = ctypes
+_SIGNATURES = {
+    "tcx_last_error": (_c.c_char_p, []),
+    "tcx_version": (_c.c_char_p, []),
+    "tcx_leaf_policy": (_c.c_int, [_c.c_uint64, _c.c_uint64, _c.POINTER(_c.c_uint64)]),
+    "tcx_sha256_leaves": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_uint64, _c.c_void_p, _c.c_uint64, _c.c_void_p]),
+    "tcx_merkle_scratch_bytes": (_c.c_uint64, [_c.c_uint64]),
+    "tcx_merkle_root": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_void_p]),
+    "tcx_multihash_encode": (_c.c_int, [_c.c_void_p, _c.c_char_p, _c.c_size_t]),
+    "tcx_multihash_from_gpu": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_int, _c.c_uint64, _c.c_char_p, _c.c_size_t]),
+    "tcx_prewarm_device": (_c.c_int, [_c.c_int]),
+    "tcx_prewarm_visible_devices": (_c.c_int, []),
+}
+
+
+def lib(build_if_missing: bool = True):
+    """Load libtcx.so (building it first if it is absent and nvcc is available)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                if not build_if_missing:
+                    raise RuntimeError(f"libtcx is not built ({LIB_PATH} missing)")
+                build_native()
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point and raise TcxError on failure."""
+    L = lib()
+    rc = getattr(L, name)(*args)
+    if rc != OK:
+        _raise(rc)
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
