@@ -1,0 +1,530 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 realization hot path (TensorCast from_disk load + GPU SHA-256).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tcx|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+Workload (BASELINE configs[1] at N=1, its tensor-parallel form at N>1): a synthetic
+Llama-3-8B-shaped bf16 safetensors artifact (seed 1, 16 060 522 496 payload bytes) in
+tmpfs. Each rank stages its leaf-aligned 1/N of the canonical byte space, hashes the
+leaves it staged (SHA-256, explicit 4 MiB leaves), the ranks exchange over NVLink the
+bytes of each other's tensor-parallel view (N=1: the identity view), and every rank
+ends with its view and the verified Merkle root of the whole artifact.
+
+One JSON line on rank 0:
+* value  - realized GB/s (artifact bytes / step) with the staged bytes already in HBM
+           (device-timed, max over ranks);
+* e2e    - the same metric through tcx_group_load from pinned host memory (H2D, hashing,
+           exchange, view, 32-byte root read-back all inside the timed step);
+* roofline - the SHA-256 leaf kernel against the measured compute bound of the
+           compression (register-only probe) and the measured HBM bandwidth;
+* cpu_baseline - the reference's CPU path (pread + OpenSSL SHA-256 per leaf + Merkle
+           tree, single thread, source_hash.cc:19-61) restated in oracle/, on a sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Realized GB/s into 1/2/4/8 B200 (SHA-256 verified); GPU SHA-256 GB/s/GPU"
+LEAF = 4 << 20
+SEED = 1
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["tcx", "reference"], default="tcx")
+    ap.add_argument("--dir", default=os.environ.get("TCX_BENCH_DIR", "/dev/shm/tcx_bench"))
+    ap.add_argument("--model", choices=["llama3-8b", "llama3-70b"], default="llama3-8b")
+    ap.add_argument("--leaf", type=int, default=LEAF)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU baseline sample time")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--hash-only", metavar="BYTES:LEAF",
+                    help="only time the SHA-256 leaf kernel on BYTES of seeded device data (e.g. 512M:128K); "
+                         "the small case used for ncu captures")
+    return ap.parse_args()
+
+
+def _size(x: str) -> int:
+    mult = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}
+    return int(float(x[:-1]) * mult[x[-1].upper()]) if x[-1].upper() in mult else int(x)
+
+
+def run_hash_only(args) -> None:
+    import torch
+    import tensorcast_b200 as tcx
+    nbytes, leaf = (_size(v) for v in args.hash_only.split(":"))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    src = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda", generator=g)
+    n = (nbytes + leaf - 1) // leaf
+    out = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        tcx.sha256_leaves(src, leaf, out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        tcx.sha256_leaves(src, leaf, out)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"mode": "hash-only", "bytes": nbytes, "leaf": leaf, "leaves": n, "ms": round(ms, 3),
+                      "gbs": round(nbytes / ms / 1e6, 2)}), flush=True)
+
+
+def log(*a):
+    print("[bench]", *a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Artifact
+# ---------------------------------------------------------------------------
+def artifact_path(args) -> str:
+    return os.path.join(args.dir, f"{args.model}-seed{SEED}.safetensors")
+
+
+def ensure_artifact(args, rank: int, local_rank: int) -> str:
+    """Rank 0 writes the artifact once (marker file); the other ranks wait for it."""
+    from tensorcast_b200.synthetic import LLAMA3_70B, LLAMA3_8B, artifact_bytes, llama_shapes, write_safetensors
+    cfg = LLAMA3_8B if args.model == "llama3-8b" else LLAMA3_70B
+    shapes = llama_shapes(cfg)
+    path = artifact_path(args)
+    marker = path + ".done"
+    if rank == 0 and not os.path.exists(marker):
+        import torch
+        os.makedirs(args.dir, exist_ok=True)
+        need = artifact_bytes(shapes) + (64 << 20)
+        st = os.statvfs(args.dir)
+        if st.f_bavail * st.f_frsize < need:
+            raise SystemExit(f"not enough space in {args.dir} for the {need / 1e9:.1f} GB artifact "
+                             f"(set TCX_BENCH_DIR)")
+        t0 = time.time()
+        dev = f"cuda:{local_rank}" if torch.cuda.is_available() else "cpu"
+        info = write_safetensors(path, shapes, SEED, device=dev)
+        with open(marker, "w") as f:
+            json.dump(info, f)
+        log(f"wrote {info['total_bytes'] / 1e9:.2f} GB artifact in {time.time() - t0:.1f}s ({dev})")
+    t0 = time.time()
+    while not os.path.exists(marker):
+        if time.time() - t0 > 900:
+            raise SystemExit("timed out waiting for rank 0 to write the artifact")
+        time.sleep(0.5)
+    return path
+
+
+def tp_slices(index, world: int, rank: int) -> dict:
+    """BASELINE TP sharding: q/k/v/gate/up, embed and lm_head along dim 0; o/down along dim 1."""
+    out = {}
+    for name, e in index.entries.items():
+        if any(k in name for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj", "embed_tokens", "lm_head")):
+            d = 0
+        elif any(k in name for k in ("o_proj", "down_proj")):
+            d = 1
+        else:
+            continue
+        ln = e.shape[d] // world
+        out[name] = (d, slice(rank * ln, (rank + 1) * ln))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, device: int):
+        self.device, self.proc, self.rows = device, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == len(self.FIELDS):
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        pw = [float(r[3]) for r in self.rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows), "power_w_max": max(pw) if pw else None}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the reference's CPU hashing path, restated in oracle/)
+# ---------------------------------------------------------------------------
+def cpu_reference_sample(path: str, payload_off: int, total: int, leaf: int, target_s: float,
+                         max_bytes: int | None = None) -> dict:
+    """pread of a leaf-aligned sample of the canonical bytes + OpenSSL SHA-256 per leaf
+    (single thread, source_hash.cc:38-58) + Merkle tree + multihash, timed on the host."""
+    import numpy as np
+    from oracle import oracle
+
+    def run(nbytes):
+        buf = np.empty(nbytes, np.uint8)
+        t0 = time.perf_counter()
+        with open(path, "rb", buffering=0) as f:
+            f.seek(payload_off)
+            mv = memoryview(buf)
+            got = 0
+            while got < nbytes:
+                n = f.readinto(mv[got:])
+                if not n:
+                    raise IOError("short read")
+                got += n
+        d = oracle.leaf_digests(buf, leaf, openssl=True, threads=1)
+        oracle.multihash(oracle.tree_root(d))
+        return time.perf_counter() - t0
+
+    probe = min(total, 64 * leaf)
+    dt = run(probe)
+    rate = probe / dt
+    nbytes = min(total, max(probe, int(rate * target_s) // leaf * leaf))
+    if max_bytes:
+        nbytes = min(nbytes, max_bytes)
+    dt = run(nbytes)
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"first {nbytes // leaf} leaves ({nbytes / 1e9:.2f} GB) of the artifact: pread from tmpfs + "
+                      f"OpenSSL EVP SHA-256 per {leaf >> 20} MiB leaf + Merkle tree, 1 thread",
+            "seconds": round(dt, 2), "host_nproc": os.cpu_count()}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    path = ensure_artifact(args, 0, int(os.environ.get("LOCAL_RANK", "0")))
+    from tensorcast_b200.artifact import build_canonical_index, build_source_index, canonical_segments
+    index = build_canonical_index(build_source_index(path))
+    segs = canonical_segments(index, 0, index.total_bytes)
+    payload_off = segs[0][1]
+    if len(segs) != 1:
+        raise SystemExit("canonical bytes are not one contiguous payload range")
+    per_step = max(args.cpu_seconds / max(args.steps, 1), 2.0)
+    for _ in range(args.warmup):
+        cpu_reference_sample(path, payload_off, index.total_bytes, args.leaf, min(per_step, 2.0))
+    vals = [cpu_reference_sample(path, payload_off, index.total_bytes, args.leaf, per_step) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in vals)
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(statistics.median(x["seconds"] for x in vals) * 1e3, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{args.model} safetensors from tmpfs, SHA-256 {args.leaf >> 20} MiB leaves, "
+                                   f"CPU realization sample (reference CPU hashing path)",
+                       "artifact_bytes": index.total_bytes, "leaf_bytes": args.leaf},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": vals[0]["sample"]},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# tcx arm
+# ---------------------------------------------------------------------------
+def main() -> None:
+    args = parse_args()
+    if args.hash_only:
+        run_hash_only(args)
+        return
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"note: WORLD_SIZE={world} differs from --gpus {args.gpus}; using WORLD_SIZE")
+    torch.cuda.set_device(local)
+    path = ensure_artifact(args, rank, local)
+    if world > 1:
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    import tensorcast_b200 as tcx
+    from tensorcast_b200 import _native
+    from tensorcast_b200.artifact import build_canonical_index, build_source_index, canonical_segments, pad_ranges
+    from tensorcast_b200.loader import Group, read_segments, stage_bounds
+    from tensorcast_b200.views import build_view_spec, plan_view
+
+    index = build_canonical_index(build_source_index(path))
+    T, L = index.total_bytes, args.leaf
+    bounds = stage_bounds(T, L, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    whole = canonical_segments(index, 0, T)
+    canonical_is_payload = len(whole) == 1 and whole[0][3] == T
+    # Every rank's view: identity at N=1, the tensor-parallel shards otherwise.
+    plans = []
+    for r in range(world):
+        spec = None if world == 1 else build_view_spec(index, slices=tp_slices(index, world, r))
+        plans.append(plan_view(index, spec))
+    mine = plans[rank]
+    rank_jobs = [p.jobs for p in plans]
+
+    # Staged bytes: tmpfs -> pinned host memory (setup, timed separately).
+    t0 = time.perf_counter()
+    h_stage = torch.empty(hi - lo, dtype=torch.uint8, pin_memory=True)
+    t_pin = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    read_segments(canonical_segments(index, lo, hi), h_stage.data_ptr(), threads=min(32, os.cpu_count() or 8))
+    for off, ln in pad_ranges(index, lo, hi):
+        h_stage[off:off + ln].zero_()
+    t_read = time.perf_counter() - t0
+    d_stage = torch.empty(hi - lo, dtype=torch.uint8, device="cuda")
+    d_stage.copy_(h_stage)
+    identity = world == 1 and mine.is_identity
+    d_view = d_stage if identity else torch.empty(max(mine.view_bytes, 1), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    group = Group.from_torch_distributed(local) if world > 1 else Group(1, 0, local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def load(host: bool, expected=None):
+        return group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage if host else None,
+                          permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # First load establishes the root; rank 0 checks it against the CPU oracle over the whole file.
+    first = load(False)
+    root = first["root"]
+    parity = {}
+    if rank == 0:
+        from oracle import oracle
+        mm = np.memmap(path, dtype=np.uint8, mode="r", offset=whole[0][1], shape=(T,)) if canonical_is_payload else None
+        if mm is not None:
+            t0 = time.perf_counter()
+            threads = os.cpu_count() or 8
+            cpu_root = oracle.tree_root(oracle.leaf_digests(mm, L, openssl=True, threads=threads))
+            parity = {"root_matches_cpu_oracle": cpu_root == root, "oracle_threads": threads,
+                      "oracle_seconds": round(time.perf_counter() - t0, 1), "multihash": first["multihash"]}
+            if cpu_root != root:
+                raise SystemExit(f"PARITY FAILURE: GPU root {root.hex()} != CPU oracle {cpu_root.hex()}")
+    # Views: check a fixed sample of tensors against numpy slicing of the file.
+    view_ok = verify_view_sample(path, index, mine, d_view, world, rank, whole)
+    if world > 1:
+        ok = torch.tensor([1 if view_ok else 0], device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        view_ok = bool(ok.item())
+    if not view_ok:
+        raise SystemExit("PARITY FAILURE: view bytes differ from numpy slicing of the artifact")
+
+    # Hash-kernel roofline (device-resident, alone, CUDA events on the launching stream).
+    hk = hash_kernel_roofline(d_stage, hi - lo, L, rank)
+
+    # value: device-resident loads.
+    for _ in range(args.warmup):
+        load(False, root)
+    with ClockSampler(local) as clk:
+        barrier()
+        n0 = _native.lib().tcx_kernel_launch_count()
+        w0 = time.perf_counter()
+        dev_ms = [load(False, root)["total_ms"] for _ in range(args.steps)]
+        barrier()
+        wall = (time.perf_counter() - w0) / args.steps * 1e3
+        launches = _native.lib().tcx_kernel_launch_count() - n0
+    ms = max_over_ranks(statistics.mean(dev_ms))
+    wall = max_over_ranks(wall)
+
+    # e2e: from pinned host memory through tcx_group_load.
+    for _ in range(args.warmup):
+        load(True, root)
+    barrier()
+    n0 = _native.lib().tcx_kernel_launch_count()
+    e2e_res = [load(True, root) for _ in range(args.steps)]
+    barrier()
+    e2e_launches = _native.lib().tcx_kernel_launch_count() - n0
+    e2e_ms = max_over_ranks(statistics.mean(r["total_ms"] for r in e2e_res))
+    h2d_ms = max_over_ranks(statistics.mean(r["h2d_ms"] for r in e2e_res))
+    peer = max_over_ranks(float(e2e_res[-1]["peer_recv_bytes"]))
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and canonical_is_payload:
+        cpu = cpu_reference_sample(path, whole[0][1], T, L, args.cpu_seconds)
+
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(T / ms / 1e6, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+            "config": {
+                "workload": (f"{args.model}-shaped bf16 safetensors (seed {SEED}), {T} B, identity view"
+                             if world == 1 else
+                             f"{args.model}-shaped bf16 safetensors (seed {SEED}), {T} B, TP-{world} views "
+                             f"(q/k/v/gate/up/embed/lm_head dim 0, o/down dim 1)"),
+                "artifact_bytes": T, "leaf_bytes": L, "leaves": first["leaves"],
+                "view_bytes_per_rank": mine.view_bytes, "parallelism": f"tp{world}",
+                "l2": "inputs (staged bytes) far larger than the 126 MB L2; no flush needed",
+                "timing": "device events per step (tcx_group_load), mean over steps, max over ranks"},
+            "sha256_gbs_per_gpu": hk["achieved"],
+            "roofline": hk,
+            "e2e": {"value": round(T / e2e_ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": hi - lo if world == 1 else T, "d2h_bytes_per_step": 32 * world,
+                    "h2d_ms": round(h2d_ms, 3), "h2d_gbs_per_gpu": round((hi - lo) / h2d_ms / 1e6, 2),
+                    "gpu_launches": int(e2e_launches)},
+            "gpu_launches": int(launches),
+            "wall_ms_per_step": round(wall, 3),
+            "phases_ms": {"hash": round(first["hash_ms"], 3), "exchange": round(first["exchange_ms"], 3)},
+            "peer_recv_bytes_per_rank": int(peer),
+            "setup": {"disk_to_pinned_gbs": round((hi - lo) / t_read / 1e9, 2), "pin_alloc_s": round(t_pin, 2),
+                      "canonical_is_payload": canonical_is_payload},
+            "parity": dict(parity, view_sample_ok=view_ok),
+            "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    group.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def verify_view_sample(path, index, plan, d_view, world, rank, whole) -> bool:
+    """Compares a deterministic sample of view tensors with numpy slicing of the file."""
+    import numpy as np
+    import torch
+    names = [t.name for t in plan.tensors]
+    pick = set(names[::37]) | {n for n in names if "embed" in n or "lm_head" in n or "layers.0." in n}
+    src = {n: index.sources[n] for n in pick}
+    ok = True
+    for t in plan.tensors:
+        if t.name not in pick:
+            continue
+        st = src[t.name]
+        arr = np.memmap(path, dtype=np.uint16, mode="r", offset=st.file_offset, shape=st.shape)
+        if world > 1:
+            e = index.entries[t.name]
+            if any(k in t.name for k in ("o_proj", "down_proj")):
+                ln = e.shape[1] // world
+                arr = arr[:, rank * ln:(rank + 1) * ln]
+            elif any(k in t.name for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj", "embed", "lm_head")):
+                ln = e.shape[0] // world
+                arr = arr[rank * ln:(rank + 1) * ln]
+        got = d_view[t.offset:t.offset + t.nbytes].cpu().numpy()
+        ok &= bool((got == np.ascontiguousarray(arr).view(np.uint8).reshape(-1)).all())
+    torch.cuda.synchronize()
+    return ok
+
+
+def hash_kernel_roofline(d_stage, nbytes: int, leaf: int, rank: int) -> dict:
+    """Times the SHA-256 leaf kernel alone over the staged bytes and the register-only probes."""
+    import torch
+    import tensorcast_b200 as tcx
+    from tensorcast_b200 import _native
+    n = (nbytes + leaf - 1) // leaf
+    out = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, reps=3):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            e0.record(s)
+            fn()
+            e1.record(s)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    ms = timed(lambda: tcx.sha256_leaves(d_stage, leaf, out, nbytes=nbytes, stream=s))
+    achieved = nbytes / ms / 1e6
+    # Compute bound: 64 chains per SMSP x 592 SMSPs, 1024 blocks each.
+    probe_n, probe_b = 148 * 4 * 64, 1024
+    pout = torch.empty((probe_n, 32), dtype=torch.uint8, device="cuda")
+    pms = timed(lambda: _native.call("tcx_sha256_compute_probe", probe_n, probe_b, pout.data_ptr(), s.cuda_stream))
+    compute = probe_n * probe_b * 64 / pms / 1e6
+    # Chain latency: one warp, 4096 blocks.
+    lms = timed(lambda: _native.call("tcx_sha256_compute_probe", 32, 4096, pout.data_ptr(), s.cuda_stream), reps=2)
+    t_block_us = lms * 1e3 / 4096
+    chain = n * 64 / (t_block_us * 1e-6) / 1e9
+    hbm = measured_hbm()
+    peak = min(compute, hbm["gbs"])
+    traffic = profiled_traffic(nbytes)
+    return {"bound": "int_alu" if compute < hbm["gbs"] else "hbm", "achieved": round(achieved, 2),
+            "peak": round(peak, 2), "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "traffic": traffic, "kernel": "sha256_leaf (ws/plain auto)", "leaves": n,
+            "algorithmic_bytes": nbytes, "kernel_ms": round(ms, 3),
+            "compute_bound_gbs": round(compute, 2), "compute_bound_source": "measured: register-only SHA-256 probe, "
+            f"{probe_n} chains x {probe_b} blocks", "hbm_gbs": hbm["gbs"], "hbm_source": hbm["source"],
+            "frac_of_hbm": round(achieved / hbm["gbs"], 4), "chain_bound_gbs": round(chain, 2),
+            "t_block_us_single_warp": round(t_block_us, 4), "frac_of_chain_bound": round(achieved / chain, 4)}
+
+
+def measured_hbm() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return {"gbs": float(json.load(f)["hbm_gbs"]), "source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
+    except Exception:
+        return {"gbs": 6650.0, "source": "profiling recipe fallback 6.65 TB/s (of fallback)"}
+
+
+def profiled_traffic(nbytes: int):
+    """DRAM bytes of one launch, scaled from the committed ncu capture of the leaf kernel."""
+    p = os.path.join(ROOT, "profiles", "sha256_leaf_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return round(d["dram_bytes_per_hashed_byte"] * nbytes)
+    except Exception:
+        return None
+
+
+if __name__ == "__main__":
+    main()

@@ -50,6 +50,10 @@ const char* tcx_last_error(void);
 /* Library version string. */
 const char* tcx_version(void);
 
+/* Number of kernels this library has launched in this process (diagnostics:
+ * lets a caller count the device work of a call). No reference counterpart. */
+uint64_t tcx_kernel_launch_count(void);
+
 /* ---------------------------------------------------------------------------
  * Content hashing (the data multihash of an artifact).
  * ------------------------------------------------------------------------ */
@@ -72,6 +76,29 @@ tcx_status tcx_leaf_policy(uint64_t total_bytes, uint64_t requested_leaf_bytes, 
  * the vectorised path. */
 tcx_status tcx_sha256_leaves(const void* d_src, uint64_t total_bytes, uint64_t leaf_bytes, void* d_digests,
                              uint64_t digest_capacity, void* stream);
+
+/* One pass of streamed per-leaf SHA-256, stream-ordered: consumes bytes
+ * [seg_off, seg_off + seg_len) of every leaf of d_src (leaf i at i*L), so a
+ * buffer can be hashed while it is still arriving (e.g. one H2D slab per pass).
+ * d_states holds 8 words per leaf and carries each chain between passes; the
+ * pass that reaches a leaf's end pads it and writes its digest to d_digests.
+ * Passes must run in order with seg_off = the previous seg_off + seg_len,
+ * starting at 0; seg_off and seg_len are multiples of 64 (seg_len may exceed
+ * the leaf). Leaves already finished are left alone. No reference
+ * counterpart: the reference hashes only fully resident buffers
+ * (core/common/artifact_hash_gpu.cc:693-826); this is the streamed form of the
+ * same per-leaf digest. Requirements otherwise as tcx_sha256_leaves, plus
+ * d_states 16-byte aligned with 32 * ceil(T/L) bytes. */
+tcx_status tcx_sha256_leaves_pass(const void* d_src, uint64_t total_bytes, uint64_t leaf_bytes, uint64_t seg_off,
+                                  uint64_t seg_len, void* d_states, void* d_digests, uint64_t digest_capacity,
+                                  void* stream);
+
+/* Calibration probe, stream-ordered: n_chains independent SHA-256 chains of
+ * `blocks` compressions each on register-resident data (no memory traffic but
+ * the 32-byte final states written to d_out). Timed by the caller, it gives the
+ * compute bound of the compression (many chains) and the per-block latency of
+ * one chain (32 chains). No reference counterpart (measurement aid). */
+tcx_status tcx_sha256_compute_probe(uint32_t n_chains, uint32_t blocks, void* d_out, void* stream);
 
 /* Scratch bytes tcx_merkle_root needs for n leaf digests. */
 uint64_t tcx_merkle_scratch_bytes(uint64_t n_leaves);
@@ -108,6 +135,164 @@ tcx_status tcx_prewarm_device(int device_id);
 /* tcx_prewarm_device for every visible device (OK when none is visible).
  * Replaces prewarm_gpu_hash_nvrtc_for_visible_devices (artifact_hash_gpu.cc:856-901). */
 tcx_status tcx_prewarm_visible_devices(void);
+
+/* ---------------------------------------------------------------------------
+ * View materialisation (tensor-parallel shards, slices and transposes).
+ * ------------------------------------------------------------------------ */
+
+#define TCX_MAX_DIMS 8
+
+/* One strided byte copy: `rows` rows of `row_bytes` bytes, row k read from
+ * src + src_off + k*src_pitch and written to dst + dst_off + k*dst_pitch.
+ * An identity or dim-0 narrowed tensor is one row; a narrow along dim d > 0 is
+ * prod(shape[:d]) rows of length*prod(shape[d+1:])*esize bytes at source pitch
+ * shape[d]*prod(shape[d+1:])*esize -- the `outer` blocks of
+ * compute_bidirectional_internal (view_planner.cc:466-524). */
+typedef struct tcx_copy_job {
+  uint64_t src_off;
+  uint64_t dst_off;
+  uint64_t src_pitch;
+  uint64_t dst_pitch;
+  uint64_t row_bytes;
+  uint64_t rows;
+} tcx_copy_job;
+
+/* A compact tensor of `shape` (element size esize) at src + src_off, written
+ * permuted to dst + dst_off: output dim i is input dim perm[i], i.e.
+ * torch permute(perm).contiguous() (view_transform_executor.cc:116-131). */
+typedef struct tcx_permute_job {
+  uint64_t src_off;
+  uint64_t dst_off;
+  uint32_t esize;
+  uint32_t ndim;
+  int64_t shape[TCX_MAX_DIMS];
+  int32_t perm[TCX_MAX_DIMS];
+} tcx_permute_job;
+
+/* Device scratch bytes tcx_copy_jobs needs for n jobs. */
+uint64_t tcx_copy_jobs_scratch_bytes(uint64_t n_jobs);
+
+/* Runs n copy jobs (d_jobs: device array) from d_src to d_dst in one
+ * stream-ordered launch pair. Destination ranges must not overlap each other
+ * or the source. Replaces the GenericByteRangeExecutor data copies and the
+ * cudaMemcpy2DAsync column packs of execute_dim1_tensor
+ * (core/store/replica/collective_disk_loader.cc:4488-4508). */
+tcx_status tcx_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* d_jobs, uint64_t n_jobs,
+                         void* d_scratch, uint64_t scratch_bytes, void* stream);
+
+/* One out-of-place permute (job in host memory), stream-ordered. Replaces the
+ * GPU branch of execute_transform
+ * (core/store/materialization/dataplane/view/view_transform_executor.cc:74-133). */
+tcx_status tcx_permute(const void* d_src, void* d_dst, const tcx_permute_job* job, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Collective from-disk load: each rank stages 1/N of the canonical byte space
+ * (leaf-aligned) into its own VRAM, hashes the leaves it staged, and the ranks
+ * exchange over NVLink (NCCL grouped send/recv) exactly the bytes each peer's
+ * view needs; every rank then holds its view and the artifact's Merkle root.
+ * Replaces try_collective_disk_load / execute_group_collective
+ * (core/store/replica/collective_disk_loader.h:120-142,
+ * collective_disk_loader.cc:5538-5816) and the verification-stage hash of the
+ * loaded replica (core/store/materialization/runtime/pipeline/
+ * verification_stage.cc:55-128).
+ * ------------------------------------------------------------------------ */
+
+#define TCX_UNIQUE_ID_BYTES 128
+
+typedef struct tcx_group tcx_group;
+
+/* A file range to read into pinned memory: `length` bytes at `file_offset` of
+ * `path` land at dst_offset of the destination buffer. */
+typedef struct tcx_file_segment {
+  const char* path;
+  uint64_t file_offset;
+  uint64_t dst_offset;
+  uint64_t length;
+} tcx_file_segment;
+
+/* Everything a rank needs to know about one collective load; identical on
+ * every rank except the buffers. */
+typedef struct tcx_load_plan {
+  uint64_t total_bytes;          /* T: size of the canonical byte space */
+  uint64_t leaf_bytes;           /* hash leaf size L (used as given) */
+  const uint64_t* stage_bounds;  /* world+1 offsets, multiples of L, bounds[world] = T:
+                                    rank r stages [bounds[r], bounds[r+1]) */
+  const tcx_copy_job* jobs;      /* every rank's view: src_off in the canonical space,
+                                    dst_off/dst_pitch in that rank's view buffer */
+  const uint64_t* job_offsets;   /* world+1: rank r's jobs are jobs[off[r], off[r+1]) */
+  const tcx_permute_job* permutes; /* this rank's in-place permutes of view regions, run
+                                      after the exchange (src_off == dst_off) */
+  uint64_t n_permutes;
+  uint64_t view_bytes;           /* bytes of this rank's view buffer */
+  uint64_t slab_bytes;           /* bytes per leaf per H2D/hash slab (0: 256 KiB) */
+} tcx_load_plan;
+
+/* Per-peer sizes and job lists of the exchange for one rank (host-only planning).
+ * Capacities: tcx_plan_exchange_capacity(). pack_jobs move this rank's staged
+ * bytes (src offsets relative to the staged range) into the send buffer;
+ * local_jobs move them straight into the view; scatter_jobs move received
+ * bytes from the receive buffer into the view, for peers whose bytes do not
+ * land contiguously (direct[p] == 0). direct[p] == 1: the bytes from peer p are
+ * received straight into the view at recv_view_off[p]. */
+typedef struct tcx_exchange_plan {
+  tcx_copy_job* pack_jobs;
+  uint64_t n_pack;
+  tcx_copy_job* local_jobs;
+  uint64_t n_local;
+  tcx_copy_job* scatter_jobs;
+  uint64_t n_scatter;
+  uint64_t* send_offsets;   /* world+1 offsets into the send buffer */
+  uint64_t* recv_offsets;   /* world+1 offsets into the receive buffer (non-direct peers) */
+  uint64_t* recv_counts;    /* world: bytes received from each peer */
+  uint64_t* recv_view_off;  /* world: view offset of a direct receive */
+  uint8_t* direct;          /* world flags */
+  uint64_t* gaps;           /* 2*capacity entries: (offset, length) pairs of view bytes no job
+                               writes; the load zero-fills them */
+  uint64_t n_gaps;
+} tcx_exchange_plan;
+
+/* Upper bound on each job count and gap count tcx_plan_exchange may produce
+ * (each job array needs this many entries, gaps twice as many). */
+uint64_t tcx_plan_exchange_capacity(const tcx_load_plan* plan, int world);
+
+/* Host-only: the exchange schedule of `rank` in a `world`-rank load. */
+tcx_status tcx_plan_exchange(const tcx_load_plan* plan, int world, int rank, tcx_exchange_plan* out);
+
+/* Reads segments into dst (pinned or pageable host memory) with `threads`
+ * parallel preads; a short read is DATA_LOSS (source_hash.cc:44-51). */
+tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n, void* dst, int threads);
+
+/* A new NCCL unique id (rank 0 creates it; the caller distributes the bytes). */
+tcx_status tcx_group_unique_id(uint8_t* out128);
+
+/* Joins rank `rank` of a `world`-rank group on CUDA device `device`
+ * (unique_id may be NULL when world == 1). Waits at most timeout_ms for the
+ * other ranks (DEADLINE_EXCEEDED, communicator aborted). Replaces the
+ * NcclClique of collective_disk_loader.cc:209-306 (one process per GPU here
+ * instead of one leader thread driving every GPU). */
+tcx_status tcx_group_create(const uint8_t* unique_id, int world, int rank, int device, int64_t timeout_ms,
+                            tcx_group** out);
+
+/* Releases the group's communicator, streams and device buffers. */
+tcx_status tcx_group_destroy(tcx_group* g);
+
+typedef struct tcx_load_result {
+  uint8_t root[32];     /* Merkle root over all ranks' leaves */
+  char multihash[64];   /* data multihash of the root (NUL terminated) */
+  uint64_t leaves;      /* total leaf count */
+  uint64_t h2d_bytes;   /* host-to-device bytes of this rank */
+  uint64_t peer_send_bytes, peer_recv_bytes;
+  float h2d_ms, hash_ms, exchange_ms, total_ms;  /* device-timed phases on this rank */
+} tcx_load_result;
+
+/* Runs one collective load on every rank of g (all ranks call it with the same
+ * plan). h_stage: this rank's staged bytes in pinned host memory, or NULL when
+ * d_stage already holds them (device-resident load: no H2D). d_view may equal
+ * d_stage when every job of this rank is an in-place identity. Synchronous.
+ * expected_root (32 bytes, may be NULL): a mismatch returns DATA_LOSS
+ * (verification_stage.cc:130-141). */
+tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage, void* d_view,
+                          const uint8_t* expected_root, tcx_load_result* out);
 
 #ifdef __cplusplus
 }

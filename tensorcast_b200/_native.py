@@ -49,19 +49,76 @@ def _raise(code: int) -> None:
     raise TcxError(code, msg)
 
 
-# Every function exported by include/tcx.h with (restype, argtypes).
 _c = ctypes
+
+
+class CopyJob(ctypes.Structure):
+    _fields_ = [("src_off", _c.c_uint64), ("dst_off", _c.c_uint64), ("src_pitch", _c.c_uint64),
+                ("dst_pitch", _c.c_uint64), ("row_bytes", _c.c_uint64), ("rows", _c.c_uint64)]
+
+
+MAX_DIMS = 8
+
+
+class PermuteJob(ctypes.Structure):
+    _fields_ = [("src_off", _c.c_uint64), ("dst_off", _c.c_uint64), ("esize", _c.c_uint32), ("ndim", _c.c_uint32),
+                ("shape", _c.c_int64 * MAX_DIMS), ("perm", _c.c_int32 * MAX_DIMS)]
+
+
+class FileSegment(ctypes.Structure):
+    _fields_ = [("path", _c.c_char_p), ("file_offset", _c.c_uint64), ("dst_offset", _c.c_uint64),
+                ("length", _c.c_uint64)]
+
+
+class LoadPlan(ctypes.Structure):
+    _fields_ = [("total_bytes", _c.c_uint64), ("leaf_bytes", _c.c_uint64), ("stage_bounds", _c.c_void_p),
+                ("jobs", _c.c_void_p), ("job_offsets", _c.c_void_p), ("permutes", _c.c_void_p),
+                ("n_permutes", _c.c_uint64), ("view_bytes", _c.c_uint64), ("slab_bytes", _c.c_uint64)]
+
+
+class ExchangePlan(ctypes.Structure):
+    _fields_ = [("pack_jobs", _c.c_void_p), ("n_pack", _c.c_uint64), ("local_jobs", _c.c_void_p),
+                ("n_local", _c.c_uint64), ("scatter_jobs", _c.c_void_p), ("n_scatter", _c.c_uint64),
+                ("send_offsets", _c.c_void_p), ("recv_offsets", _c.c_void_p), ("recv_counts", _c.c_void_p),
+                ("recv_view_off", _c.c_void_p), ("direct", _c.c_void_p), ("gaps", _c.c_void_p),
+                ("n_gaps", _c.c_uint64)]
+
+
+class LoadResult(ctypes.Structure):
+    _fields_ = [("root", _c.c_uint8 * 32), ("multihash", _c.c_char * 64), ("leaves", _c.c_uint64),
+                ("h2d_bytes", _c.c_uint64), ("peer_send_bytes", _c.c_uint64), ("peer_recv_bytes", _c.c_uint64),
+                ("h2d_ms", _c.c_float), ("hash_ms", _c.c_float), ("exchange_ms", _c.c_float),
+                ("total_ms", _c.c_float)]
+
+
+# Every function exported by include/tcx.h with (restype, argtypes).
 _SIGNATURES = {
     "tcx_last_error": (_c.c_char_p, []),
     "tcx_version": (_c.c_char_p, []),
+    "tcx_kernel_launch_count": (_c.c_uint64, []),
+    "tcx_sha256_compute_probe": (_c.c_int, [_c.c_uint32, _c.c_uint32, _c.c_void_p, _c.c_void_p]),
     "tcx_leaf_policy": (_c.c_int, [_c.c_uint64, _c.c_uint64, _c.POINTER(_c.c_uint64)]),
     "tcx_sha256_leaves": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_uint64, _c.c_void_p, _c.c_uint64, _c.c_void_p]),
+    "tcx_sha256_leaves_pass": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_uint64, _c.c_uint64, _c.c_uint64,
+                                          _c.c_void_p, _c.c_void_p, _c.c_uint64, _c.c_void_p]),
     "tcx_merkle_scratch_bytes": (_c.c_uint64, [_c.c_uint64]),
     "tcx_merkle_root": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_void_p]),
     "tcx_multihash_encode": (_c.c_int, [_c.c_void_p, _c.c_char_p, _c.c_size_t]),
     "tcx_multihash_from_gpu": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_int, _c.c_uint64, _c.c_char_p, _c.c_size_t]),
     "tcx_prewarm_device": (_c.c_int, [_c.c_int]),
     "tcx_prewarm_visible_devices": (_c.c_int, []),
+    "tcx_copy_jobs_scratch_bytes": (_c.c_uint64, [_c.c_uint64]),
+    "tcx_copy_jobs": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_uint64,
+                                 _c.c_void_p]),
+    "tcx_permute": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(PermuteJob), _c.c_void_p]),
+    "tcx_plan_exchange_capacity": (_c.c_uint64, [_c.POINTER(LoadPlan), _c.c_int]),
+    "tcx_plan_exchange": (_c.c_int, [_c.POINTER(LoadPlan), _c.c_int, _c.c_int, _c.POINTER(ExchangePlan)]),
+    "tcx_read_segments": (_c.c_int, [_c.POINTER(FileSegment), _c.c_uint64, _c.c_void_p, _c.c_int]),
+    "tcx_group_unique_id": (_c.c_int, [_c.c_void_p]),
+    "tcx_group_create": (_c.c_int, [_c.c_void_p, _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.POINTER(_c.c_void_p)]),
+    "tcx_group_destroy": (_c.c_int, [_c.c_void_p]),
+    "tcx_group_load": (_c.c_int, [_c.c_void_p, _c.POINTER(LoadPlan), _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                  _c.c_void_p, _c.POINTER(LoadResult)]),
 }
 
 

@@ -61,7 +61,7 @@ def build_native(force: bool = False, verbose: bool = False) -> str:
         subprocess.check_call(cmd)
         objs.append(obj)
     tmp = LIB_PATH + ".tmp"
-    link = [nvcc, *ARCH_FLAGS, "-shared", "-o", tmp, *objs, "-lpthread"]
+    link = [nvcc, *ARCH_FLAGS, "-shared", "-o", tmp, *objs, "-lnccl", "-lpthread"]
     if verbose:
         print(" ".join(link), file=sys.stderr)
     subprocess.check_call(link)

@@ -8,12 +8,23 @@
 //   * leaf policy determine_leaf_chunk_size (artifact_hash_cpu.cc:269-303).
 //
 // Kernel design. SHA-256 is serial inside a leaf, so the unit of parallelism is
-// the leaf: one thread owns one leaf's chain and keeps the state, the 16-word
-// message window and the next block (prefetched one block ahead) in registers.
-// Loads are 16-byte non-allocating vector loads; no shared memory is used.
+// the leaf ("chain"). Two kernels:
+//   * sha256_leaf_kernel: one thread owns one chain and keeps the state, the
+//     16-word message window and the next block in registers. Best when there
+//     are enough chains to fill every SM sub-partition (SMSP) several times.
+//   * sha256_leaf_ws_kernel (warp-specialised): a consumer warp runs only the
+//     64 compression rounds of 32 chains while a producer warp on another SMSP
+//     loads the blocks, expands the message schedule and adds the round
+//     constants, handing K[t]+W[t] over through a double-buffered shared-memory
+//     ring guarded by named barriers. With few chains (large leaves) the chain's
+//     own instruction stream is the limit, and this removes ~40% of it.
+// Both take a pass window [seg_off, seg_off+seg_len) inside every leaf and a
+// per-chain state array, so a leaf can be hashed in several passes as its bytes
+// arrive (streamed loads); a single pass with seg_off = 0 covers the whole leaf.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -37,19 +48,75 @@ constexpr int kFinishThreads = 1024;
 // same aligned 4-byte word as at least one byte of the leaf, so no read can leave
 // the pages of the buffer.
 // ---------------------------------------------------------------------------
+// Per-chain quantities of one pass. A pass covers [seg_off, seg_off + seg_len) of
+// every leaf (seg_off and, unless it reaches the leaf end, seg_len are multiples
+// of 64). The chain is finalised in the pass that reaches its end.
+struct LeafPass {
+  uint64_t leaf_len;  // bytes of this leaf
+  uint64_t begin;     // first byte of the pass inside the leaf
+  uint64_t nfull;     // full 64-byte blocks of leaf data in this pass
+  uint32_t nb;        // blocks compressed in this pass (data + padding)
+  bool active;        // the pass touches this leaf
+  bool finalize;      // the pass reaches the leaf end: pad and emit the digest
+};
+
+__device__ __forceinline__ LeafPass leaf_pass(uint32_t i, uint32_t n_leaves, uint64_t total, uint64_t leaf,
+                                              uint64_t seg_off, uint64_t seg_len) {
+  LeafPass p{};
+  if (i >= n_leaves) return p;
+  const uint64_t off = static_cast<uint64_t>(i) * leaf;
+  p.leaf_len = min(leaf, total - off);
+  if (seg_off >= p.leaf_len) return p;
+  p.active = true;
+  p.begin = seg_off;
+  const uint64_t room = p.leaf_len - seg_off;
+  p.finalize = seg_len >= room;
+  const uint64_t bytes = p.finalize ? room : seg_len;
+  p.nfull = bytes >> 6;
+  p.nb = static_cast<uint32_t>(p.nfull) + (p.finalize ? ((p.leaf_len & 63u) < 56u ? 1u : 2u) : 0u);
+  return p;
+}
+
+__device__ __forceinline__ void load_or_init_state(uint32_t s[8], const LeafPass& p, const uint32_t* states,
+                                                   uint32_t i) {
+  if (p.begin == 0 || states == nullptr) {
+    dev::init_state(s);
+  } else {
+    const uint4* st = reinterpret_cast<const uint4*>(states + 8ull * i);
+    const uint4 x = st[0], y = st[1];
+    s[0] = x.x; s[1] = x.y; s[2] = x.z; s[3] = x.w;
+    s[4] = y.x; s[5] = y.y; s[6] = y.z; s[7] = y.w;
+  }
+}
+
+__device__ __forceinline__ void save_state(const uint32_t s[8], uint32_t* states, uint32_t i) {
+  uint4* st = reinterpret_cast<uint4*>(states + 8ull * i);
+  st[0] = make_uint4(s[0], s[1], s[2], s[3]);
+  st[1] = make_uint4(s[4], s[5], s[6], s[7]);
+}
+
+// ---------------------------------------------------------------------------
+// Plain leaf kernel: one thread per chain.
+// kVec: every leaf start is 16-byte aligned (16-aligned base, L % 16 == 0).
+// Otherwise each leaf start has a fixed misalignment s = addr & 3 and a block is
+// assembled from 17 aligned words with funnel shifts. Every word read lies in the
+// same aligned 4-byte word as at least one byte of the leaf, so no read can leave
+// the pages of the buffer.
+// ---------------------------------------------------------------------------
 template <bool kVec>
 __global__ void __launch_bounds__(kLeafThreads) sha256_leaf_kernel(const uint8_t* __restrict__ src, uint64_t total,
                                                                    uint64_t leaf, uint32_t n_leaves,
+                                                                   uint64_t seg_off, uint64_t seg_len,
+                                                                   uint32_t* __restrict__ states,
                                                                    uint8_t* __restrict__ digests) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_leaves) return;
-  const uint64_t off = static_cast<uint64_t>(i) * leaf;
-  const uint64_t len = min(leaf, total - off);
-  const uint8_t* p = src + off;
-  const uint64_t nfull = len >> 6;
+  const LeafPass ps = leaf_pass(i, n_leaves, total, leaf, seg_off, seg_len);
+  if (!ps.active) return;
+  const uint8_t* p = src + static_cast<uint64_t>(i) * leaf + ps.begin;
+  const uint64_t nfull = ps.nfull;
 
   uint32_t s[8];
-  dev::init_state(s);
+  load_or_init_state(s, ps, states, i);
   uint32_t w[16];
 
   if constexpr (kVec) {
@@ -89,8 +156,215 @@ __global__ void __launch_bounds__(kLeafThreads) sha256_leaf_kernel(const uint8_t
       dev::compress(s, w);
     }
   }
-  dev::finish(s, p + (nfull << 6), static_cast<uint32_t>(len & 63u), len);
-  dev::store_digest(digests + 32ull * i, s);
+  if (ps.finalize) {
+    dev::finish(s, p + (nfull << 6), static_cast<uint32_t>(ps.leaf_len & 63u), ps.leaf_len);
+    dev::store_digest(digests + 32ull * i, s);
+  } else {
+    save_state(s, states, i);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Warp-specialised leaf kernel (16-byte aligned leaves only).
+// CTA = kWsPairs consumer warps (warps 0..P-1) + kWsPairs producer warps
+// (warps P..2P-1); producer warp P+c feeds consumer warp c, lane j <-> chain j.
+// Shared ring per pair: kWsStages stages x kWsBlocks blocks x 64 words x 32 lanes,
+// laid out [stage][block][t/4][lane][t%4] so that each lane moves 16 bytes per
+// access and a warp touches 512 contiguous bytes (no bank conflicts).
+// ---------------------------------------------------------------------------
+constexpr int kWsPairs = 2;
+constexpr int kWsStages = 2;
+constexpr int kWsBlocks = 2;  // blocks per stage
+constexpr int kWsThreads = 64 * kWsPairs;
+constexpr int kWsBlockWords = 64 * 32;
+constexpr int kWsStageWords = kWsBlocks * kWsBlockWords;
+constexpr size_t kWsSmemBytes = static_cast<size_t>(kWsPairs) * kWsStages * kWsStageWords * 4;
+
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Message words of block b of a pass: data (b < nfull), the padded tail, or the
+// length-only block; zero for blocks past the chain's end.
+__device__ __forceinline__ void ws_tail_words(uint32_t w[16], const LeafPass& ps, const uint8_t* p, uint32_t b) {
+  const uint32_t rem = static_cast<uint32_t>(ps.leaf_len & 63u);
+  const uint64_t bits = ps.leaf_len * 8ull;
+  const bool tail = ps.finalize && b == ps.nfull;
+  const bool len_only = ps.finalize && rem >= 56 && b == ps.nfull + 1;
+  const uint8_t* t = p + (ps.nfull << 6);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t pos = 4u * k + j;
+      uint32_t byte = 0;
+      if (tail) {
+        if (pos < rem) {
+          byte = t[pos];
+        } else if (pos == rem) {
+          byte = 0x80u;
+        }
+      }
+      word |= byte << (24 - 8 * j);
+    }
+    w[k] = word;
+  }
+  if ((tail && rem < 56) || len_only) {
+    w[14] = static_cast<uint32_t>(bits >> 32);
+    w[15] = static_cast<uint32_t>(bits);
+  }
+}
+
+__device__ __forceinline__ void ws_produce_block(uint4* dst, uint32_t w[16], uint32_t lane) {
+  // K[t] + W[t] for the 64 rounds, four rounds per 16-byte store.
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    uint32_t kw[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = 4 * q + r;
+      if (t >= 16) {
+        w[t & 15] += dev::small_sigma1(w[(t - 2) & 15]) + w[(t - 7) & 15] + dev::small_sigma0(w[(t - 15) & 15]);
+      }
+      kw[r] = dev::kRoundK[t] + w[t & 15];
+    }
+    dst[q * 32 + lane] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+  }
+}
+
+__device__ __forceinline__ void ws_consume_block(uint32_t s[8], const uint4* src, uint32_t lane, bool keep) {
+  uint32_t a = s[0], b = s[1], c = s[2], d = s[3], e = s[4], f = s[5], g = s[6], h = s[7];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const uint4 kw4 = src[q * 32 + lane];
+    const uint32_t kw[4] = {kw4.x, kw4.y, kw4.z, kw4.w};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint32_t t1 = h + kw[r] + dev::big_sigma1(e) + dev::choose(e, f, g);
+      const uint32_t t2 = dev::big_sigma0(a) + dev::majority(a, b, c);
+      h = g;
+      g = f;
+      f = e;
+      e = d + t1;
+      d = c;
+      c = b;
+      b = a;
+      a = t1 + t2;
+    }
+  }
+  if (keep) {
+    s[0] += a; s[1] += b; s[2] += c; s[3] += d;
+    s[4] += e; s[5] += f; s[6] += g; s[7] += h;
+  }
+}
+
+__global__ void __launch_bounds__(kWsThreads, 1) sha256_leaf_ws_kernel(const uint8_t* __restrict__ src,
+                                                                       uint64_t total, uint64_t leaf,
+                                                                       uint32_t n_leaves, uint64_t seg_off,
+                                                                       uint64_t seg_len,
+                                                                       uint32_t* __restrict__ states,
+                                                                       uint8_t* __restrict__ digests) {
+  extern __shared__ uint4 ws_smem[];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const bool producer = warp >= kWsPairs;
+  const uint32_t pair = producer ? warp - kWsPairs : warp;
+  const uint32_t i = blockIdx.x * (32u * kWsPairs) + pair * 32u + lane;
+  const LeafPass ps = leaf_pass(i, n_leaves, total, leaf, seg_off, seg_len);
+  const uint32_t max_nb = __reduce_max_sync(0xffffffffu, ps.active ? ps.nb : 0u);
+  const uint32_t n_stages = (max_nb + kWsBlocks - 1) / kWsBlocks;
+  uint4* ring = ws_smem + static_cast<size_t>(pair) * kWsStages * (kWsStageWords / 4);
+  const uint32_t bar_full = 1u + pair * 2u * kWsStages;
+  const uint32_t bar_empty = bar_full + kWsStages;
+
+  if (producer) {
+    const uint8_t* p = src + (ps.active ? static_cast<uint64_t>(i) * leaf + ps.begin : 0ull);
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+    uint4 cur[4], nxt[4];
+    if (ps.active && ps.nfull > 0) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cur[k] = dev::ldg_stream(q + k);
+    }
+    if (ps.active && ps.nfull > 1) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) nxt[k] = dev::ldg_stream(q + 4 + k);
+    }
+    uint32_t b = 0;
+    for (uint32_t st = 0; st < n_stages; ++st) {
+      const uint32_t slot = st % kWsStages;
+      named_bar_sync(bar_empty + slot, 64);
+      uint4* stage = ring + static_cast<size_t>(slot) * (kWsStageWords / 4);
+#pragma unroll 1
+      for (int blk = 0; blk < kWsBlocks; ++blk, ++b) {
+        if (b >= max_nb) break;
+        uint32_t w[16];
+        if (ps.active && b < ps.nfull) {
+          dev::words_from_vec(w, cur[0], cur[1], cur[2], cur[3]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
+          if (b + 2 < ps.nfull) {
+            const uint4* nq = q + 4ull * (b + 2);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) nxt[k] = dev::ldg_stream(nq + k);
+          }
+        } else {
+          ws_tail_words(w, ps, p, b);
+        }
+        ws_produce_block(stage + blk * (kWsBlockWords / 4), w, lane);
+      }
+      named_bar_arrive(bar_full + slot, 64);
+    }
+    // Match the consumer's trailing releases so every barrier generation completes.
+    for (uint32_t st = n_stages; st < n_stages + kWsStages; ++st) named_bar_sync(bar_empty + st % kWsStages, 64);
+  } else {
+    uint32_t s[8];
+    load_or_init_state(s, ps, states, i);
+    for (int k = 0; k < kWsStages; ++k) named_bar_arrive(bar_empty + k, 64);
+    uint32_t b = 0;
+    for (uint32_t st = 0; st < n_stages; ++st) {
+      const uint32_t slot = st % kWsStages;
+      named_bar_sync(bar_full + slot, 64);
+      const uint4* stage = ring + static_cast<size_t>(slot) * (kWsStageWords / 4);
+#pragma unroll 1
+      for (int blk = 0; blk < kWsBlocks; ++blk, ++b) {
+        if (b >= max_nb) break;
+        ws_consume_block(s, stage + blk * (kWsBlockWords / 4), lane, ps.active && b < ps.nb);
+      }
+      named_bar_arrive(bar_empty + slot, 64);
+    }
+    if (ps.active) {
+      if (ps.finalize) {
+        dev::store_digest(digests + 32ull * i, s);
+      } else {
+        save_state(s, states, i);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Register-only compression throughput probe: n chains x `blocks` compressions
+// whose message words are derived from the running state (so nothing can be
+// hoisted), no memory traffic except the final state. Measures the SHA-256
+// compute bound (and, with one warp, the per-block chain latency) of this GPU.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kLeafThreads) sha256_probe_kernel(uint32_t n, uint32_t blocks, uint32_t* out) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  uint32_t s[8], w[16];
+  dev::init_state(s);
+  s[0] ^= i;
+  for (uint32_t b = 0; b < blocks; ++b) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) w[k] = s[k & 7] + static_cast<uint32_t>(k) + b;
+    dev::compress(s, w);
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + 8ull * i);
+  o[0] = make_uint4(s[0], s[1], s[2], s[3]);
+  o[1] = make_uint4(s[4], s[5], s[6], s[7]);
 }
 
 // ---------------------------------------------------------------------------
@@ -192,18 +466,58 @@ uint64_t leaf_policy(uint64_t total, uint64_t requested) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-tcx_status launch_leaves(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, void* d_digests,
-                         cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>(div_up(n, kLeafThreads)));
+}  // namespace
+
+// Chains up to which the warp-specialised kernel is chosen (one wave of CTAs
+// with a consumer and a producer warp per SMSP pair).
+static constexpr uint32_t kWsMaxChains = 148u * 32u * kWsPairs * 2u;
+
+static int hash_kernel_choice() {
+  // TCX_HASH_KERNEL=plain|ws|auto (default auto) selects the leaf kernel.
+  const char* v = std::getenv("TCX_HASH_KERNEL");
+  if (v == nullptr) return 0;
+  if (std::strcmp(v, "plain") == 0) return 1;
+  if (std::strcmp(v, "ws") == 0) return 2;
+  return 0;
+}
+
+tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, uint64_t seg_off,
+                            uint64_t seg_len, uint32_t* states, void* d_digests, cudaStream_t stream) {
   const auto* src = static_cast<const uint8_t*>(d_src);
   auto* out = static_cast<uint8_t*>(d_digests);
-  if (aligned16(d_src) && leaf % 16 == 0) {
-    sha256_leaf_kernel<true><<<grid, kLeafThreads, 0, stream>>>(src, total, leaf, n, out);
+  const bool vec = aligned16(d_src) && leaf % 16 == 0;
+  const int choice = hash_kernel_choice();
+  const bool ws = vec && (choice == 2 || (choice == 0 && n <= kWsMaxChains));
+  if (ws) {
+    static thread_local int configured_device = -1;
+    int dev = 0;
+    TCX_CUDA_TRY(cudaGetDevice(&dev));
+    if (configured_device != dev) {
+      TCX_CUDA_TRY(cudaFuncSetAttribute(sha256_leaf_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(kWsSmemBytes)));
+      configured_device = dev;
+    }
+    const dim3 grid(static_cast<unsigned>(div_up(n, 32u * kWsPairs)));
+    sha256_leaf_ws_kernel<<<grid, kWsThreads, kWsSmemBytes, stream>>>(src, total, leaf, n, seg_off, seg_len,
+                                                                       states, out);
+    note_launches(1);
+  } else if (vec) {
+    const dim3 grid(static_cast<unsigned>(div_up(n, kLeafThreads)));
+    sha256_leaf_kernel<true><<<grid, kLeafThreads, 0, stream>>>(src, total, leaf, n, seg_off, seg_len, states, out);
+    note_launches(1);
   } else {
-    sha256_leaf_kernel<false><<<grid, kLeafThreads, 0, stream>>>(src, total, leaf, n, out);
+    const dim3 grid(static_cast<unsigned>(div_up(n, kLeafThreads)));
+    sha256_leaf_kernel<false><<<grid, kLeafThreads, 0, stream>>>(src, total, leaf, n, seg_off, seg_len, states,
+                                                                 out);
+    note_launches(1);
   }
   TCX_CUDA_TRY(cudaGetLastError());
   return TCX_OK;
+}
+
+tcx_status launch_leaves(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, void* d_digests,
+                         cudaStream_t stream) {
+  return launch_leaf_pass(d_src, total, leaf, n, 0, ~0ull, nullptr, d_digests, stream);
 }
 
 uint64_t merkle_scratch_bytes(uint64_t n) {
@@ -222,6 +536,7 @@ tcx_status launch_merkle(const uint8_t* digests, uint64_t n, uint8_t* scratch, u
     const uint64_t next = div_up(m, 2);
     const unsigned grid = static_cast<unsigned>(div_up(next, kMerkleThreads));
     merkle_level_kernel<<<grid, kMerkleThreads, 0, stream>>>(cur, static_cast<uint32_t>(m), buf[which]);
+    note_launches(1);
     TCX_CUDA_TRY(cudaGetLastError());
     cur = buf[which];
     which ^= 1;
@@ -234,6 +549,7 @@ tcx_status launch_merkle(const uint8_t* digests, uint64_t n, uint8_t* scratch, u
                                       static_cast<int>(kFinishMax * 32)));
   }
   merkle_finish_kernel<<<1, kFinishThreads, smem, stream>>>(cur, static_cast<uint32_t>(m), root);
+  note_launches(1);
   TCX_CUDA_TRY(cudaGetLastError());
   return TCX_OK;
 }
@@ -258,6 +574,8 @@ void encode_multihash(const uint8_t digest[32], char out[57]) {
   std::memcpy(out + 1, tmp, 55);  // ceil(34 * 8 / 5) = 55 significant characters
   out[56] = '\0';
 }
+
+namespace {
 
 // Per-device resources of tcx_multihash_from_gpu, created once and grown on demand.
 struct DeviceHashContext {
@@ -284,6 +602,7 @@ tcx_status ensure_context(DeviceHashContext& ctx, uint64_t n_leaves) {
     cudaFuncAttributes attr;
     TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_kernel<true>));
     TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_kernel<false>));
+    TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_ws_kernel));
     TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, merkle_level_kernel));
     ctx.ready = true;
   }
@@ -325,8 +644,10 @@ extern "C" tcx_status tcx_leaf_policy(uint64_t total_bytes, uint64_t requested_l
   return TCX_OK;
 }
 
-extern "C" tcx_status tcx_sha256_leaves(const void* d_src, uint64_t total_bytes, uint64_t leaf_bytes,
-                                        void* d_digests, uint64_t digest_capacity, void* stream) {
+namespace tcx {
+namespace {
+tcx_status check_leaf_args(const void* d_src, uint64_t total_bytes, uint64_t leaf_bytes, void* d_digests,
+                           uint64_t digest_capacity) {
   if (d_src == nullptr) return set_error(TCX_INVALID_ARGUMENT, "GPU pointer is null");
   if (total_bytes == 0) return set_error(TCX_INVALID_ARGUMENT, "Cannot hash empty GPU buffer");
   if (total_bytes > TCX_MAX_HASH_BYTES)
@@ -343,8 +664,44 @@ extern "C" tcx_status tcx_sha256_leaves(const void* d_src, uint64_t total_bytes,
   if (digest_capacity < n)
     return set_errorf(TCX_INVALID_ARGUMENT, "digest buffer holds %llu digests, %llu needed",
                       static_cast<unsigned long long>(digest_capacity), static_cast<unsigned long long>(n));
+  return TCX_OK;
+}
+}  // namespace
+}  // namespace tcx
+
+extern "C" tcx_status tcx_sha256_leaves(const void* d_src, uint64_t total_bytes, uint64_t leaf_bytes,
+                                        void* d_digests, uint64_t digest_capacity, void* stream) {
+  tcx_status st = check_leaf_args(d_src, total_bytes, leaf_bytes, d_digests, digest_capacity);
+  if (st != TCX_OK) return st;
+  const uint64_t n = div_up(total_bytes, leaf_bytes);
   return launch_leaves(d_src, total_bytes, leaf_bytes, static_cast<uint32_t>(n), d_digests,
                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" tcx_status tcx_sha256_leaves_pass(const void* d_src, uint64_t total_bytes, uint64_t leaf_bytes,
+                                             uint64_t seg_off, uint64_t seg_len, void* d_states, void* d_digests,
+                                             uint64_t digest_capacity, void* stream) {
+  if (seg_off % 64 != 0 || seg_len % 64 != 0 || seg_len == 0)
+    return set_error(TCX_INVALID_ARGUMENT, "seg_off and seg_len must be non-zero multiples of 64");
+  if (d_states == nullptr || !aligned16(d_states))
+    return set_error(TCX_INVALID_ARGUMENT, "state buffer must be non-null and 16-byte aligned");
+  // Same argument checks as the single-pass entry point.
+  tcx_status st = check_leaf_args(d_src, total_bytes, leaf_bytes, d_digests, digest_capacity);
+  if (st != TCX_OK) return st;
+  const uint64_t n = div_up(total_bytes, leaf_bytes);
+  return launch_leaf_pass(d_src, total_bytes, leaf_bytes, static_cast<uint32_t>(n), seg_off, seg_len,
+                          static_cast<uint32_t*>(d_states), d_digests, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" tcx_status tcx_sha256_compute_probe(uint32_t n_chains, uint32_t blocks, void* d_out, void* stream) {
+  if (n_chains == 0 || d_out == nullptr || !aligned16(d_out))
+    return set_error(TCX_INVALID_ARGUMENT, "n_chains > 0 and a 16-byte aligned output are required");
+  const dim3 grid(static_cast<unsigned>(div_up(n_chains, kLeafThreads)));
+  sha256_probe_kernel<<<grid, kLeafThreads, 0, static_cast<cudaStream_t>(stream)>>>(n_chains, blocks,
+                                                                                   static_cast<uint32_t*>(d_out));
+  note_launches(1);
+  TCX_CUDA_TRY(cudaGetLastError());
+  return TCX_OK;
 }
 
 extern "C" uint64_t tcx_merkle_scratch_bytes(uint64_t n_leaves) { return merkle_scratch_bytes(n_leaves); }

@@ -1,0 +1,500 @@
+// Collective load engine: one process (one tcx_group) per GPU.
+//
+// Per rank, three streams carry the pipeline of tcx_group_load:
+//   copy:  pinned host -> HBM of this rank's staged range, in slabs laid across
+//          all of its leaves at once (one 2-D copy per slab: width = slab,
+//          pitch = leaf), so every leaf's SHA-256 chain advances as soon as a
+//          slab lands instead of leaves completing one after another;
+//   hash:  one streamed SHA-256 pass per slab over all leaves of the range;
+//   comm:  after the last slab: zero-fill of view gaps, pack of each peer's
+//          bytes, local extraction into the view, one NCCL group of
+//          send/recv (personalised all-to-all over NVLink), scatter of
+//          non-contiguous receives, in-place permutes; then the leaf digests
+//          of all ranks (NCCL all-gather), the Merkle root and a 32-byte
+//          device-to-host read.
+// Reference: collective_disk_loader.cc:5538-5816 runs read -> H2D to one root
+// GPU -> ncclBroadcast/ncclSend per chunk with a host synchronize after every
+// chunk; verification_stage.cc:55-128 hashes the replica afterwards.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <nccl.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "tcx_internal.h"
+
+namespace tcx {
+tcx_status validate_load_plan(const tcx_load_plan* plan, int world);
+}
+
+namespace {
+
+using namespace tcx;
+using Clock = std::chrono::steady_clock;
+
+constexpr uint64_t kDefaultSlab = 256 * 1024;
+
+std::string nccl_msg(ncclResult_t r) { return std::string(ncclGetErrorString(r)); }
+
+struct DevBuf {
+  void* p = nullptr;
+  uint64_t cap = 0;
+  tcx_status grow(uint64_t bytes) {
+    if (bytes <= cap) return TCX_OK;
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    const uint64_t want = std::max<uint64_t>(bytes, 256);
+    if (cudaError_t e = cudaMalloc(&p, want); e != cudaSuccess) {
+      return set_errorf(TCX_RESOURCE_EXHAUSTED, "cudaMalloc(%llu) failed: %s",
+                        static_cast<unsigned long long>(want), cuda_msg(e).c_str());
+    }
+    cap = want;
+    return TCX_OK;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+  uint8_t* bytes() const { return static_cast<uint8_t*>(p); }
+};
+
+}  // namespace
+
+struct tcx_group {
+  int world = 1, rank = 0, device = 0;
+  int64_t timeout_ms = 60000;
+  ncclComm_t comm = nullptr;
+  cudaStream_t s_copy = nullptr, s_hash = nullptr, s_comm = nullptr;
+  DevBuf digests_mine, states, digests_all, digests_compact, merkle_scratch, root, send, recv, perm_scratch, jobs,
+      prefix;
+  uint8_t* h_root = nullptr;
+  tcx_copy_job* h_jobs = nullptr;
+  uint64_t h_jobs_cap = 0;
+  std::vector<cudaEvent_t> slab_events;
+  cudaEvent_t ev_start = nullptr, ev_h2d = nullptr, ev_hash = nullptr, ev_exch = nullptr, ev_end = nullptr;
+};
+
+namespace {
+
+// Waits until a non-blocking communicator has no operation in progress.
+tcx_status nccl_settle(tcx_group* g, Clock::time_point deadline, const char* what) {
+  for (;;) {
+    ncclResult_t state = ncclSuccess;
+    ncclResult_t r = ncclCommGetAsyncError(g->comm, &state);
+    if (r != ncclSuccess) return set_errorf(TCX_INTERNAL, "%s: ncclCommGetAsyncError: %s", what, nccl_msg(r).c_str());
+    if (state == ncclSuccess) return TCX_OK;
+    if (state != ncclInProgress) return set_errorf(TCX_INTERNAL, "%s: %s", what, nccl_msg(state).c_str());
+    if (Clock::now() > deadline) {
+      ncclCommAbort(g->comm);
+      g->comm = nullptr;
+      return set_errorf(TCX_DEADLINE_EXCEEDED, "%s: timed out waiting for peers", what);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+tcx_status nccl_check(tcx_group* g, ncclResult_t r, Clock::time_point deadline, const char* what) {
+  if (r == ncclSuccess) return TCX_OK;
+  if (r == ncclInProgress) return nccl_settle(g, deadline, what);
+  return set_errorf(TCX_INTERNAL, "%s: %s", what, nccl_msg(r).c_str());
+}
+
+// Waits for ev with a deadline, watching the communicator for asynchronous errors.
+tcx_status wait_event(tcx_group* g, cudaEvent_t ev, Clock::time_point deadline) {
+  if (g->comm == nullptr) {
+    TCX_CUDA_TRY(cudaEventSynchronize(ev));
+    return TCX_OK;
+  }
+  for (;;) {
+    cudaError_t e = cudaEventQuery(ev);
+    if (e == cudaSuccess) return TCX_OK;
+    if (e != cudaErrorNotReady) return set_error(TCX_INTERNAL, "load failed on the device: " + cuda_msg(e));
+    ncclResult_t state = ncclSuccess;
+    ncclCommGetAsyncError(g->comm, &state);
+    if (state != ncclSuccess && state != ncclInProgress) {
+      ncclCommAbort(g->comm);
+      g->comm = nullptr;
+      return set_errorf(TCX_INTERNAL, "NCCL error during load: %s", nccl_msg(state).c_str());
+    }
+    if (Clock::now() > deadline) {
+      ncclCommAbort(g->comm);
+      g->comm = nullptr;
+      return set_error(TCX_DEADLINE_EXCEEDED, "collective load timed out (a peer did not take part)");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+float elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
+  float ms = 0;
+  if (cudaEventElapsedTime(&ms, a, b) != cudaSuccess) return -1.f;
+  return ms;
+}
+
+}  // namespace
+
+extern "C" tcx_status tcx_group_unique_id(uint8_t* out128) {
+  if (out128 == nullptr) return set_error(TCX_INVALID_ARGUMENT, "out is null");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return set_errorf(TCX_INTERNAL, "ncclGetUniqueId: %s", nccl_msg(r).c_str());
+  static_assert(sizeof(id) == TCX_UNIQUE_ID_BYTES, "NCCL unique id size");
+  std::memcpy(out128, &id, sizeof id);
+  return TCX_OK;
+}
+
+extern "C" tcx_status tcx_group_create(const uint8_t* unique_id, int world, int rank, int device, int64_t timeout_ms,
+                                       tcx_group** out) {
+  if (out == nullptr) return set_error(TCX_INVALID_ARGUMENT, "out is null");
+  *out = nullptr;
+  if (world < 1 || rank < 0 || rank >= world) return set_error(TCX_INVALID_ARGUMENT, "rank/world out of range");
+  if (world > 1 && unique_id == nullptr) return set_error(TCX_INVALID_ARGUMENT, "unique_id is required for world > 1");
+  if (cudaError_t e = cudaSetDevice(device); e != cudaSuccess)
+    return set_errorf(TCX_INTERNAL, "Failed to set CUDA device %d: %s", device, cuda_msg(e).c_str());
+  auto* g = new tcx_group();
+  g->world = world;
+  g->rank = rank;
+  g->device = device;
+  g->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+  auto fail = [&](tcx_status st) {
+    tcx_group_destroy(g);
+    return st;
+  };
+  if (cudaStreamCreateWithFlags(&g->s_copy, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&g->s_hash, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&g->s_comm, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(set_error(TCX_INTERNAL, "stream creation failed"));
+  for (cudaEvent_t* ev : {&g->ev_start, &g->ev_h2d, &g->ev_hash, &g->ev_exch, &g->ev_end})
+    if (cudaEventCreate(ev) != cudaSuccess) return fail(set_error(TCX_INTERNAL, "event creation failed"));
+  if (cudaMallocHost(&g->h_root, 256) != cudaSuccess) return fail(set_error(TCX_INTERNAL, "pinned alloc failed"));
+  if (world > 1) {
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof id);
+    ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+    config.blocking = 0;
+    const auto deadline = Clock::now() + std::chrono::milliseconds(g->timeout_ms);
+    ncclResult_t r = ncclCommInitRankConfig(&g->comm, world, id, rank, &config);
+    if (r != ncclSuccess && r != ncclInProgress)
+      return fail(set_errorf(TCX_INTERNAL, "ncclCommInitRankConfig: %s", nccl_msg(r).c_str()));
+    tcx_status st = nccl_settle(g, deadline, "communicator init");
+    if (st != TCX_OK) return fail(st);
+  }
+  *out = g;
+  return TCX_OK;
+}
+
+extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
+  if (g == nullptr) return TCX_OK;
+  cudaSetDevice(g->device);
+  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm})
+    if (s) cudaStreamSynchronize(s);
+  if (g->comm) {
+    ncclCommFinalize(g->comm);
+    const auto deadline = Clock::now() + std::chrono::milliseconds(g->timeout_ms);
+    if (nccl_settle(g, deadline, "communicator finalize") == TCX_OK && g->comm) ncclCommDestroy(g->comm);
+    g->comm = nullptr;
+  }
+  for (DevBuf* b : {&g->digests_mine, &g->states, &g->digests_all, &g->digests_compact, &g->merkle_scratch, &g->root,
+                    &g->send, &g->recv, &g->perm_scratch, &g->jobs, &g->prefix})
+    b->release();
+  if (g->h_root) cudaFreeHost(g->h_root);
+  if (g->h_jobs) cudaFreeHost(g->h_jobs);
+  for (cudaEvent_t e : g->slab_events) cudaEventDestroy(e);
+  for (cudaEvent_t e : {g->ev_start, g->ev_h2d, g->ev_hash, g->ev_exch, g->ev_end})
+    if (e) cudaEventDestroy(e);
+  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm})
+    if (s) cudaStreamDestroy(s);
+  delete g;
+  return TCX_OK;
+}
+
+extern "C" tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n, void* dst, int threads) {
+  if (n == 0) return TCX_OK;
+  if (segs == nullptr || dst == nullptr) return set_error(TCX_INVALID_ARGUMENT, "null pointer");
+  // Split every segment into <= 64 MiB pieces and spread them over the threads.
+  struct Piece {
+    const char* path;
+    uint64_t file_off, dst_off, len;
+  };
+  std::vector<Piece> pieces;
+  constexpr uint64_t kPiece = 64ull << 20;
+  for (uint64_t i = 0; i < n; ++i)
+    for (uint64_t o = 0; o < segs[i].length; o += kPiece)
+      pieces.push_back({segs[i].path, segs[i].file_offset + o, segs[i].dst_offset + o,
+                        std::min(kPiece, segs[i].length - o)});
+  const int nt = std::max(1, std::min<int>(threads, static_cast<int>(pieces.size())));
+  std::atomic<uint64_t> next{0};
+  std::atomic<int> status{TCX_OK};
+  std::vector<std::string> errors(nt);
+  auto worker = [&](int t) {
+    std::string open_path;
+    int fd = -1;
+    for (uint64_t k = next++; k < pieces.size() && status.load() == TCX_OK; k = next++) {
+      const Piece& p = pieces[k];
+      if (fd < 0 || open_path != p.path) {
+        if (fd >= 0) close(fd);
+        fd = open(p.path, O_RDONLY | O_CLOEXEC);
+        open_path = p.path;
+        if (fd < 0) {
+          errors[t] = std::string("open failed: ") + p.path;
+          status = TCX_NOT_FOUND;
+          break;
+        }
+      }
+      uint64_t got = 0;
+      while (got < p.len) {
+        const ssize_t r = pread(fd, static_cast<uint8_t*>(dst) + p.dst_off + got, p.len - got, p.file_off + got);
+        if (r <= 0) {
+          errors[t] = std::string("short read while loading source: ") + p.path;
+          status = TCX_DATA_LOSS;
+          break;
+        }
+        got += static_cast<uint64_t>(r);
+      }
+    }
+    if (fd >= 0) close(fd);
+  };
+  std::vector<std::thread> pool;
+  for (int t = 1; t < nt; ++t) pool.emplace_back(worker, t);
+  worker(0);
+  for (auto& th : pool) th.join();
+  if (status != TCX_OK) {
+    for (const auto& e : errors)
+      if (!e.empty()) return set_error(status, e);
+  }
+  return status;
+}
+
+extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage,
+                                     void* d_view, const uint8_t* expected_root, tcx_load_result* out) {
+  if (g == nullptr) return set_error(TCX_INVALID_ARGUMENT, "group is null");
+  if (g->world > 1 && g->comm == nullptr)
+    return set_error(TCX_FAILED_PRECONDITION, "group communicator was aborted by an earlier failure");
+  tcx_status st = validate_load_plan(plan, g->world);
+  if (st != TCX_OK) return st;
+  if (d_stage == nullptr || d_view == nullptr || out == nullptr)
+    return set_error(TCX_INVALID_ARGUMENT, "d_stage, d_view and out are required");
+  TCX_CUDA_TRY(cudaSetDevice(g->device));
+  const int world = g->world, rank = g->rank;
+  const uint64_t* b = plan->stage_bounds;
+  const uint64_t L = plan->leaf_bytes, T = plan->total_bytes;
+  const uint64_t lo = b[rank], hi = b[rank + 1], mine = hi - lo;
+  auto n_of = [&](int r) { return (b[r + 1] - b[r] + L - 1) / L; };
+  const uint64_t n_mine = n_of(rank);
+  uint64_t max_n = 0;
+  for (int r = 0; r < world; ++r) max_n = std::max(max_n, n_of(r));
+  const uint64_t n_total = (T + L - 1) / L;
+  if (n_total > 0xffffffffull) return set_error(TCX_INVALID_ARGUMENT, "Leaf count exceeds supported range");
+
+  // --- host planning ------------------------------------------------------
+  const uint64_t cap = tcx_plan_exchange_capacity(plan, world);
+  std::vector<tcx_copy_job> pack(cap), local(cap), scatter(cap);
+  std::vector<uint64_t> send_off(world + 1), recv_off(world + 1), recv_counts(world), recv_view(world), gaps(2 * cap);
+  std::vector<uint8_t> direct(world);
+  tcx_exchange_plan xp{pack.data(), 0, local.data(), 0, scatter.data(), 0, send_off.data(), recv_off.data(),
+                       recv_counts.data(), recv_view.data(), direct.data(), gaps.data(), 0};
+  st = tcx_plan_exchange(plan, world, rank, &xp);
+  if (st != TCX_OK) return st;
+  // A view buffer may alias the staged buffer only for a one-rank load whose
+  // local copies are all in place (an identity view): nothing is then copied,
+  // and gap zero-fill waits for the hash passes that read the same bytes.
+  const auto* vb = static_cast<const uint8_t*>(d_view);
+  const auto* sb = static_cast<const uint8_t*>(d_stage);
+  const bool alias = vb < sb + std::max<uint64_t>(mine, 1) && sb < vb + std::max<uint64_t>(plan->view_bytes, 1);
+  std::vector<tcx_copy_job> local_kept;
+  for (uint64_t i = 0; i < xp.n_local; ++i) {
+    const tcx_copy_job& j = local[i];
+    const bool in_place = d_view == d_stage && j.src_off == j.dst_off && (j.rows == 1 || j.src_pitch == j.dst_pitch);
+    if (!in_place) local_kept.push_back(j);
+  }
+  if (alias && (world > 1 || !local_kept.empty() || d_view != d_stage))
+    return set_error(TCX_INVALID_ARGUMENT, "d_view may alias d_stage only for a one-rank identity view");
+  std::vector<tcx_copy_job> compact;
+  if (world > 1) {
+    for (int r = 0; r < world; ++r) {
+      const uint64_t nr = n_of(r);
+      if (nr == 0) continue;
+      compact.push_back({static_cast<uint64_t>(r) * max_n * 32, (b[r] / L) * 32, nr * 32, nr * 32, nr * 32, 1});
+    }
+  }
+  uint64_t perm_bytes = 0;
+  for (uint64_t i = 0; i < plan->n_permutes; ++i) {
+    const tcx_permute_job& pj = plan->permutes[i];
+    st = check_permute(pj);
+    if (st != TCX_OK) return st;
+    if (pj.src_off != pj.dst_off) return set_error(TCX_INVALID_ARGUMENT, "load permutes are in place (src_off == dst_off)");
+    uint64_t bytes = pj.esize;
+    for (uint32_t d = 0; d < pj.ndim; ++d) bytes *= static_cast<uint64_t>(pj.shape[d]);
+    if (pj.dst_off + bytes > plan->view_bytes) return set_error(TCX_INVALID_ARGUMENT, "permute outside the view");
+    perm_bytes = std::max(perm_bytes, bytes);
+  }
+
+  // --- buffers --------------------------------------------------------------
+  const uint64_t n_jobs_all = xp.n_pack + local_kept.size() + xp.n_scatter + compact.size();
+  if ((st = g->digests_mine.grow(std::max<uint64_t>(max_n, 1) * 32)) != TCX_OK) return st;
+  if ((st = g->states.grow(std::max<uint64_t>(n_mine, 1) * 32)) != TCX_OK) return st;
+  if ((st = g->merkle_scratch.grow(merkle_scratch_bytes(n_total))) != TCX_OK) return st;
+  if ((st = g->root.grow(256)) != TCX_OK) return st;
+  if ((st = g->jobs.grow(std::max<uint64_t>(n_jobs_all, 1) * sizeof(tcx_copy_job))) != TCX_OK) return st;
+  if ((st = g->prefix.grow((std::max<uint64_t>(n_jobs_all, 1) + 1) * 8)) != TCX_OK) return st;
+  if (send_off[world] && (st = g->send.grow(send_off[world])) != TCX_OK) return st;
+  if (recv_off[world] && (st = g->recv.grow(recv_off[world])) != TCX_OK) return st;
+  if (perm_bytes && (st = g->perm_scratch.grow(perm_bytes)) != TCX_OK) return st;
+  if (world > 1) {
+    if ((st = g->digests_all.grow(static_cast<uint64_t>(world) * max_n * 32)) != TCX_OK) return st;
+    if ((st = g->digests_compact.grow(n_total * 32)) != TCX_OK) return st;
+  }
+  if (n_jobs_all > g->h_jobs_cap) {
+    if (g->h_jobs) cudaFreeHost(g->h_jobs);
+    g->h_jobs = nullptr;
+    g->h_jobs_cap = 0;
+    TCX_CUDA_TRY(cudaMallocHost(&g->h_jobs, n_jobs_all * sizeof(tcx_copy_job)));
+    g->h_jobs_cap = n_jobs_all;
+  }
+  tcx_copy_job* hj = g->h_jobs;
+  const uint64_t o_pack = 0, o_local = xp.n_pack, o_scatter = o_local + local_kept.size(),
+                 o_compact = o_scatter + xp.n_scatter;
+  std::copy(pack.begin(), pack.begin() + xp.n_pack, hj + o_pack);
+  std::copy(local_kept.begin(), local_kept.end(), hj + o_local);
+  std::copy(scatter.begin(), scatter.begin() + xp.n_scatter, hj + o_scatter);
+  std::copy(compact.begin(), compact.end(), hj + o_compact);
+  auto* dj = static_cast<tcx_copy_job*>(g->jobs.p);
+  auto* dprefix = static_cast<uint64_t*>(g->prefix.p);
+  auto* view = static_cast<uint8_t*>(d_view);
+  auto* stage = static_cast<uint8_t*>(d_stage);
+  const auto* hstage = static_cast<const uint8_t*>(h_stage);
+
+  const auto deadline = Clock::now() + std::chrono::milliseconds(g->timeout_ms);
+
+  // --- H2D + hashing ---------------------------------------------------------
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_start, g->s_copy));
+  TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_hash, g->ev_start, 0));
+  TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->ev_start, 0));
+  uint64_t h2d_bytes = 0;
+  if (mine > 0) {
+    if (hstage != nullptr) {
+      uint64_t S = plan->slab_bytes ? plan->slab_bytes : kDefaultSlab;
+      S = std::max<uint64_t>(64, S - S % 64);
+      const uint64_t n_full = mine / L, tail = mine - n_full * L;
+      const uint64_t span = n_full > 0 ? L : tail;  // bytes per leaf to cover
+      const uint64_t J = (span + S - 1) / S;
+      while (g->slab_events.size() < J) {
+        cudaEvent_t e;
+        TCX_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        g->slab_events.push_back(e);
+      }
+      for (uint64_t j = 0; j < J; ++j) {
+        const uint64_t off = j * S;
+        if (n_full > 0 && off < L) {
+          const uint64_t w = std::min(S, L - off);
+          TCX_CUDA_TRY(cudaMemcpy2DAsync(stage + off, L, hstage + off, L, w, n_full, cudaMemcpyHostToDevice, g->s_copy));
+        }
+        if (tail > off) {
+          const uint64_t w = std::min(S, tail - off);
+          TCX_CUDA_TRY(cudaMemcpyAsync(stage + n_full * L + off, hstage + n_full * L + off, w, cudaMemcpyHostToDevice,
+                                       g->s_copy));
+        }
+        TCX_CUDA_TRY(cudaEventRecord(g->slab_events[j], g->s_copy));
+        TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_hash, g->slab_events[j], 0));
+        st = launch_leaf_pass(stage, mine, L, static_cast<uint32_t>(n_mine), off, S,
+                              static_cast<uint32_t*>(g->states.p), g->digests_mine.p, g->s_hash);
+        if (st != TCX_OK) return st;
+      }
+      h2d_bytes = mine;
+    } else {
+      st = launch_leaf_pass(stage, mine, L, static_cast<uint32_t>(n_mine), 0, ~0ull, nullptr, g->digests_mine.p,
+                            g->s_hash);
+      if (st != TCX_OK) return st;
+    }
+  }
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_h2d, g->s_copy));
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_hash, g->s_hash));
+
+  // --- exchange and view extraction ------------------------------------------
+  TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, alias ? g->ev_hash : g->ev_h2d, 0));
+  if (n_jobs_all > 0)
+    TCX_CUDA_TRY(cudaMemcpyAsync(dj, hj, n_jobs_all * sizeof(tcx_copy_job), cudaMemcpyHostToDevice, g->s_comm));
+  for (uint64_t k = 0; k < xp.n_gaps; ++k)
+    TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
+  if (xp.n_pack && (st = launch_copy_jobs(stage, g->send.p, dj + o_pack, xp.n_pack, dprefix, g->s_comm)) != TCX_OK)
+    return st;
+  if (!local_kept.empty() &&
+      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), dprefix, g->s_comm)) != TCX_OK)
+    return st;
+  uint64_t sent = 0, received = 0;
+  if (world > 1) {
+    if ((st = nccl_check(g, ncclGroupStart(), deadline, "ncclGroupStart")) != TCX_OK) return st;
+    for (int p = 0; p < world; ++p) {
+      if (p == rank) continue;
+      const uint64_t scount = send_off[p + 1] - send_off[p];
+      if (scount) {
+        st = nccl_check(g, ncclSend(g->send.bytes() + send_off[p], scount, ncclUint8, p, g->comm, g->s_comm), deadline,
+                        "ncclSend");
+        if (st != TCX_OK) return st;
+        sent += scount;
+      }
+      if (recv_counts[p]) {
+        uint8_t* dst = direct[p] ? view + recv_view[p] : g->recv.bytes() + recv_off[p];
+        st = nccl_check(g, ncclRecv(dst, recv_counts[p], ncclUint8, p, g->comm, g->s_comm), deadline, "ncclRecv");
+        if (st != TCX_OK) return st;
+        received += recv_counts[p];
+      }
+    }
+    if ((st = nccl_check(g, ncclGroupEnd(), deadline, "exchange")) != TCX_OK) return st;
+    if (xp.n_scatter &&
+        (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter, xp.n_scatter, dprefix, g->s_comm)) != TCX_OK)
+      return st;
+  }
+  for (uint64_t i = 0; i < plan->n_permutes; ++i) {
+    tcx_permute_job pj = plan->permutes[i];
+    uint64_t bytes = pj.esize;
+    for (uint32_t d = 0; d < pj.ndim; ++d) bytes *= static_cast<uint64_t>(pj.shape[d]);
+    const uint64_t off = pj.dst_off;
+    pj.src_off = off;
+    pj.dst_off = 0;
+    if ((st = launch_permute(view, g->perm_scratch.p, pj, g->s_comm)) != TCX_OK) return st;
+    TCX_CUDA_TRY(cudaMemcpyAsync(view + off, g->perm_scratch.p, bytes, cudaMemcpyDeviceToDevice, g->s_comm));
+  }
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_exch, g->s_comm));
+
+  // --- digests of every rank, Merkle root ------------------------------------
+  TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->ev_hash, 0));
+  const uint8_t* leaf_digests = g->digests_mine.bytes();
+  if (world > 1) {
+    st = nccl_check(g, ncclAllGather(g->digests_mine.p, g->digests_all.p, max_n * 32, ncclUint8, g->comm, g->s_comm),
+                    deadline, "digest all-gather");
+    if (st != TCX_OK) return st;
+    if ((st = launch_copy_jobs(g->digests_all.p, g->digests_compact.p, dj + o_compact, compact.size(), dprefix,
+                               g->s_comm)) != TCX_OK)
+      return st;
+    leaf_digests = g->digests_compact.bytes();
+  }
+  if ((st = launch_merkle(leaf_digests, n_total, g->merkle_scratch.bytes(), g->root.bytes(), g->s_comm)) != TCX_OK)
+    return st;
+  TCX_CUDA_TRY(cudaMemcpyAsync(g->h_root, g->root.p, 32, cudaMemcpyDeviceToHost, g->s_comm));
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_end, g->s_comm));
+  if ((st = wait_event(g, g->ev_end, deadline)) != TCX_OK) return st;
+
+  std::memset(out, 0, sizeof *out);
+  std::memcpy(out->root, g->h_root, 32);
+  encode_multihash(out->root, out->multihash);
+  out->leaves = n_total;
+  out->h2d_bytes = h2d_bytes;
+  out->peer_send_bytes = sent;
+  out->peer_recv_bytes = received;
+  out->h2d_ms = elapsed_ms(g->ev_start, g->ev_h2d);
+  out->hash_ms = elapsed_ms(g->ev_start, g->ev_hash);
+  out->exchange_ms = elapsed_ms(g->ev_h2d, g->ev_exch);
+  out->total_ms = elapsed_ms(g->ev_start, g->ev_end);
+  if (expected_root != nullptr && std::memcmp(expected_root, out->root, 32) != 0)
+    return set_error(TCX_DATA_LOSS, "ARTIFACT_ID_MISMATCH: data multihash of the loaded bytes differs from the expected one");
+  return TCX_OK;
+}

@@ -18,6 +18,20 @@ tcx_status set_error(tcx_status code, const std::string& msg);
 tcx_status set_errorf(tcx_status code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 void clear_error();
 
+// Counts kernel launches of this library (tcx_kernel_launch_count).
+void note_launches(uint64_t n);
+
+// Kernel launchers shared between translation units (stream-ordered).
+tcx_status launch_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* d_jobs, uint64_t n_jobs,
+                            uint64_t* d_prefix, cudaStream_t stream);
+tcx_status launch_permute(const void* d_src, void* d_dst, const tcx_permute_job& pj, cudaStream_t stream);
+tcx_status check_permute(const tcx_permute_job& pj);
+tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, uint64_t seg_off,
+                            uint64_t seg_len, uint32_t* states, void* d_digests, cudaStream_t stream);
+tcx_status launch_merkle(const uint8_t* digests, uint64_t n, uint8_t* scratch, uint8_t* root, cudaStream_t stream);
+uint64_t merkle_scratch_bytes(uint64_t n);
+void encode_multihash(const uint8_t digest[32], char out[57]);
+
 inline std::string cuda_msg(cudaError_t e) {
   return std::string(cudaGetErrorName(e)) + ": " + cudaGetErrorString(e);
 }

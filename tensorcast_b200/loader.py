@@ -1,0 +1,151 @@
+"""Collective load: Python face of tcx_group_* (include/tcx.h).
+
+A ``Group`` is one rank of an N-rank load, one process per GPU. Ranks agree on a
+leaf-aligned split of the canonical byte space (``stage_bounds``); each stages its
+part, hashes the leaves it staged, and the native engine exchanges exactly the bytes
+each peer's view needs (NCCL grouped send/recv). All ranks end with their view and
+the Merkle root of the whole artifact.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+import torch
+
+from . import _native
+from .views import JOB_DTYPE, permute_array
+
+
+def stage_bounds(total: int, leaf: int, world: int) -> list[int]:
+    """Leaf-aligned split of [0, total) into `world` contiguous ranges (rank r stages
+    leaves [r*n//world, (r+1)*n//world))."""
+    n = (total + leaf - 1) // leaf
+    b = [min(total, ((r * n) // world) * leaf) for r in range(world)] + [total]
+    b[0] = 0
+    return b
+
+
+def _jobs_concat(rank_jobs: list) -> tuple[np.ndarray, np.ndarray]:
+    arrs = [np.ascontiguousarray(j, dtype=JOB_DTYPE) for j in rank_jobs]
+    offs = np.zeros(len(arrs) + 1, np.uint64)
+    for i, a in enumerate(arrs):
+        offs[i + 1] = offs[i] + a.size
+    jobs = np.concatenate(arrs) if arrs and offs[-1] > 0 else np.zeros(1, JOB_DTYPE)
+    return jobs, offs
+
+
+class _Plan:
+    """A tcx_load_plan with its arrays kept alive."""
+
+    def __init__(self, total, leaf, bounds, rank_jobs, permutes=(), view_bytes=0, slab_bytes=0):
+        self.bounds = np.ascontiguousarray(bounds, dtype=np.uint64)
+        self.jobs, self.job_offsets = _jobs_concat(rank_jobs)
+        self.perms = permute_array(list(permutes)) if permutes else None
+        self.c = _native.LoadPlan(
+            total_bytes=int(total), leaf_bytes=int(leaf), stage_bounds=self.bounds.ctypes.data,
+            jobs=self.jobs.ctypes.data, job_offsets=self.job_offsets.ctypes.data,
+            permutes=self.perms.ctypes.data if self.perms is not None else None,
+            n_permutes=0 if self.perms is None else len(self.perms), view_bytes=int(view_bytes),
+            slab_bytes=int(slab_bytes))
+
+
+def plan_exchange(total, leaf, bounds, rank_jobs, rank, view_bytes=0) -> dict:
+    """Host-only exchange schedule of `rank` (tcx_plan_exchange), as numpy arrays."""
+    world = len(bounds) - 1
+    plan = _Plan(total, leaf, bounds, rank_jobs, view_bytes=view_bytes)
+    L = _native.lib()
+    cap = int(L.tcx_plan_exchange_capacity(ctypes.byref(plan.c), world))
+    out = {k: np.zeros(cap, JOB_DTYPE) for k in ("pack", "local", "scatter")}
+    for k, n in (("send_offsets", world + 1), ("recv_offsets", world + 1), ("recv_counts", world),
+                 ("recv_view_off", world)):
+        out[k] = np.zeros(n, np.uint64)
+    out["direct"] = np.zeros(world, np.uint8)
+    out["gaps"] = np.zeros(2 * cap, np.uint64)
+    xp = _native.ExchangePlan(out["pack"].ctypes.data, 0, out["local"].ctypes.data, 0, out["scatter"].ctypes.data, 0,
+                              out["send_offsets"].ctypes.data, out["recv_offsets"].ctypes.data,
+                              out["recv_counts"].ctypes.data, out["recv_view_off"].ctypes.data,
+                              out["direct"].ctypes.data, out["gaps"].ctypes.data, 0)
+    _native.call("tcx_plan_exchange", ctypes.byref(plan.c), world, rank, ctypes.byref(xp))
+    out["pack"] = out["pack"][: xp.n_pack].copy()
+    out["local"] = out["local"][: xp.n_local].copy()
+    out["scatter"] = out["scatter"][: xp.n_scatter].copy()
+    out["gaps"] = out["gaps"][: 2 * xp.n_gaps].reshape(-1, 2).copy()
+    return out
+
+
+def read_segments(segments, dst_ptr: int, threads: int = 8) -> None:
+    """Parallel preads of (path, file_offset, dst_offset, length) segments into dst_ptr."""
+    if not segments:
+        return
+    arr = (_native.FileSegment * len(segments))()
+    keep = []
+    for i, (path, foff, doff, ln) in enumerate(segments):
+        p = os.fsencode(path)
+        keep.append(p)
+        arr[i] = _native.FileSegment(p, foff, doff, ln)
+    _native.call("tcx_read_segments", arr, len(segments), dst_ptr, int(threads))
+
+
+class Group:
+    """One rank of a collective load (tcx_group)."""
+
+    def __init__(self, world: int = 1, rank: int = 0, device: int = 0, unique_id: bytes | None = None,
+                 timeout_ms: int = 120_000):
+        self.world, self.rank, self.device = world, rank, device
+        self._h = ctypes.c_void_p()
+        uid = None
+        if world > 1:
+            if unique_id is None or len(unique_id) != 128:
+                raise ValueError("a 128-byte NCCL unique id is required for world > 1")
+            uid = ctypes.create_string_buffer(bytes(unique_id), 128)
+        _native.call("tcx_group_create", uid, world, rank, device, int(timeout_ms), ctypes.byref(self._h))
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        _native.call("tcx_group_unique_id", buf)
+        return buf.raw
+
+    @classmethod
+    def from_torch_distributed(cls, device: int, timeout_ms: int = 120_000) -> "Group":
+        """Builds the group over the ranks of the default torch.distributed process group
+        (the unique id travels through it)."""
+        import torch.distributed as dist
+        world, rank = dist.get_world_size(), dist.get_rank()
+        obj = [cls.unique_id() if rank == 0 else None]
+        if world > 1:
+            dist.broadcast_object_list(obj, src=0)
+        return cls(world, rank, device, obj[0] if world > 1 else None, timeout_ms)
+
+    def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, permutes=(), view_bytes=None,
+             expected_root: bytes | None = None, slab_bytes: int = 0) -> dict:
+        """Runs one load; returns the result fields as a dict. h_stage None: device-resident."""
+        if view_bytes is None:
+            view_bytes = d_view.numel() * d_view.element_size() if isinstance(d_view, torch.Tensor) else 0
+        plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes)
+        res = _native.LoadResult()
+        exp = None
+        if expected_root is not None:
+            if len(expected_root) != 32:
+                raise ValueError("expected_root must be 32 bytes")
+            exp = ctypes.create_string_buffer(bytes(expected_root), 32)
+        ptr = lambda x: None if x is None else (x.data_ptr() if isinstance(x, torch.Tensor) else int(x))  # noqa: E731
+        _native.call("tcx_group_load", self._h, ctypes.byref(plan.c), ptr(h_stage), ptr(d_stage), ptr(d_view), exp,
+                     ctypes.byref(res))
+        return {"root": bytes(res.root), "multihash": res.multihash.decode(), "leaves": res.leaves,
+                "h2d_bytes": res.h2d_bytes, "peer_send_bytes": res.peer_send_bytes,
+                "peer_recv_bytes": res.peer_recv_bytes, "h2d_ms": res.h2d_ms, "hash_ms": res.hash_ms,
+                "exchange_ms": res.exchange_ms, "total_ms": res.total_ms}
+
+    def close(self) -> None:
+        if self._h:
+            _native.lib().tcx_group_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,139 @@
+"""GPU parity of the view kernels and of the single-rank collective load (tcx_group_load)
+against the numpy view oracle and the hashing oracle: byte-identical views, bit-exact roots."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from oracle import views as oviews
+from tensorcast_b200 import _native
+from tensorcast_b200.loader import Group, stage_bounds
+from tensorcast_b200.views import JOB_DTYPE, ViewSpec, NarrowOp, TransposeOp, plan_view, permute_array
+from viewtools import index_from_meta, random_tensors, random_view
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def pinned(a: np.ndarray) -> torch.Tensor:
+    t = torch.empty(a.size, dtype=torch.uint8, pin_memory=True)
+    t.numpy()[:] = a
+    return t
+
+
+def run_copy_jobs(src: torch.Tensor, dst: torch.Tensor, jobs: np.ndarray) -> None:
+    L = _native.lib()
+    dj = dev(jobs.view(np.uint8)) if jobs.size else torch.zeros(8, dtype=torch.uint8, device="cuda")
+    sb = int(L.tcx_copy_jobs_scratch_bytes(len(jobs)))
+    scratch = torch.empty(sb, dtype=torch.uint8, device="cuda")
+    _native.call("tcx_copy_jobs", src.data_ptr(), dst.data_ptr(), dj.data_ptr(), len(jobs), scratch.data_ptr(), sb,
+                 torch.cuda.current_stream().cuda_stream)
+
+
+def test_copy_jobs_and_permutes_match_oracle(cuda_device):
+    for seed in range(12):
+        canon, meta = oviews.canonical_bytes(random_tensors(seed))
+        index = index_from_meta(meta, canon.size)
+        rng = np.random.default_rng(seed)
+        slices, transpose, subset, spec = random_view(meta, rng)
+        plan = plan_view(index, spec, subset)
+        src = dev(canon)
+        view = torch.zeros(max(plan.view_bytes, 1), dtype=torch.uint8, device="cuda")
+        run_copy_jobs(src, view, plan.jobs)
+        tmp = torch.empty_like(view)
+        for p in permute_array(plan.permutes):
+            pj = _native.PermuteJob.from_buffer_copy(p.tobytes())
+            nbytes = int(np.prod(p["shape"][: p["ndim"]])) * int(p["esize"])
+            pj.src_off, pj.dst_off = int(p["dst_off"]), 0
+            _native.call("tcx_permute", view.data_ptr(), tmp.data_ptr(), ctypes.byref(pj),
+                         torch.cuda.current_stream().cuda_stream)
+            view[int(p["dst_off"]): int(p["dst_off"]) + nbytes] = tmp[:nbytes]
+        want = oviews.materialize_view(canon, meta, slices, transpose, subset)
+        assert (view.cpu().numpy()[: plan.view_bytes] == want).all()
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 64), (4096, 1024), (130, 77), (8192, 8192), (1, 640), (640, 1)])
+def test_transpose_bf16_shapes(cuda_device, rows, cols):
+    a = np.random.default_rng(rows + cols).integers(0, 65536, size=(rows, cols), dtype=np.uint16)
+    src, out = dev(a.view(np.uint8).reshape(-1)), torch.empty(a.size * 2, dtype=torch.uint8, device="cuda")
+    pj = _native.PermuteJob(0, 0, 2, 2)
+    pj.shape[0], pj.shape[1], pj.perm[0], pj.perm[1] = rows, cols, 1, 0
+    _native.call("tcx_permute", src.data_ptr(), out.data_ptr(), ctypes.byref(pj), torch.cuda.current_stream().cuda_stream)
+    assert (out.cpu().numpy().view(np.uint16).reshape(cols, rows) == a.T).all()
+
+
+def test_streamed_passes_match_single_pass(cuda_device):
+    a = np.random.default_rng(9).integers(0, 256, size=(7 << 20) + 4133, dtype=np.uint8)
+    src = dev(a)
+    for leaf, seg in ((1 << 20, 64 << 10), (1 << 20, 192), (4096, 1 << 20), (65536 + 64, 4096)):
+        n = (a.size + leaf - 1) // leaf
+        digests = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+        states = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        for off in range(0, leaf, seg):
+            _native.call("tcx_sha256_leaves_pass", src.data_ptr(), a.size, leaf, off, seg, states.data_ptr(),
+                         digests.data_ptr(), n, s)
+        assert (digests.cpu().numpy() == oracle.leaf_digests(a, leaf, openssl=True, threads=8)).all()
+
+
+@pytest.mark.parametrize("kernel", ["plain", "ws"])
+def test_both_leaf_kernels_bit_exact(cuda_device, kernel, monkeypatch):
+    monkeypatch.setenv("TCX_HASH_KERNEL", kernel)
+    import tensorcast_b200 as tcx
+    for size, leaf in ((1, 64), (1000, 64), (1 << 20, 4096), ((3 << 20) + 57, 1 << 18), (70 << 20, 4 << 20)):
+        a = np.random.default_rng(size).integers(0, 256, size=size, dtype=np.uint8)
+        d = tcx.sha256_leaves(dev(a), leaf).cpu().numpy()
+        assert (d == oracle.leaf_digests(a, leaf, openssl=True, threads=8)).all()
+
+
+@pytest.mark.parametrize("host", [True, False])
+def test_single_rank_load_random_views(cuda_device, host):
+    g = Group(1, 0, 0)
+    try:
+        for seed in range(8):
+            canon, meta = oviews.canonical_bytes(random_tensors(seed, n=20))
+            index = index_from_meta(meta, canon.size)
+            rng = np.random.default_rng(seed)
+            slices, transpose, subset, spec = random_view(meta, rng)
+            plan = plan_view(index, spec, subset)
+            leaf = int(rng.choice([64, 256, 1024]))
+            d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+            if not host:
+                d_stage.copy_(dev(canon))
+            d_view = torch.full((max(plan.view_bytes, 1),), 0x5A, dtype=torch.uint8, device="cuda")
+            expected = oracle.tree_root(oracle.leaf_digests(canon, leaf))
+            res = g.load(canon.size, leaf, [0, canon.size], [plan.jobs], d_stage=d_stage, d_view=d_view,
+                         h_stage=pinned(canon) if host else None, permutes=plan.permutes,
+                         view_bytes=plan.view_bytes, expected_root=expected, slab_bytes=128)
+            assert res["root"] == expected
+            assert res["multihash"] == oracle.multihash(expected)
+            want = oviews.materialize_view(canon, meta, slices, transpose, subset)
+            assert (d_view.cpu().numpy()[: plan.view_bytes] == want).all()
+    finally:
+        g.close()
+
+
+def test_load_detects_corruption(cuda_device):
+    canon, meta = oviews.canonical_bytes(random_tensors(3))
+    index = index_from_meta(meta, canon.size)
+    plan = plan_view(index)
+    g = Group(1, 0, 0)
+    try:
+        expected = oracle.tree_root(oracle.leaf_digests(canon, 64))
+        bad = canon.copy()
+        bad[bad.size // 2] ^= 1
+        d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+        with pytest.raises(_native.TcxError, match="ARTIFACT_ID_MISMATCH"):
+            g.load(canon.size, 64, [0, canon.size], [plan.jobs], d_stage=d_stage, d_view=d_stage,
+                   h_stage=pinned(bad), view_bytes=plan.view_bytes, expected_root=expected)
+        res = g.load(canon.size, 64, [0, canon.size], [plan.jobs], d_stage=d_stage, d_view=d_stage,
+                     h_stage=pinned(canon), view_bytes=plan.view_bytes, expected_root=expected)
+        assert res["root"] == expected
+    finally:
+        g.close()
