@@ -1,0 +1,211 @@
+"""The reference's Python realization surface, over the native collective loader.
+
+Same names, arguments and error behaviour as the TensorCast SDK for this path:
+
+* ``from_disk(path, *, key=None, verify_checksums=True, show_progress=None)``
+  (tensorcast/api/store/__init__.py:4548-4560, method :3294-3388)
+* ``Artifact.subset(names)`` / ``Artifact.view(*, slices=None, transpose=None)`` /
+  ``Artifact.tensor_dict(*, device, options=None, ctx=None)``
+  (tensorcast/api/store/artifact.py:1779, 1765-1776, 1509-1520)
+* ``CallContext(collective=CollectiveLoadGroup(group_id, world_size, rank))``
+  (tensorcast/api/context.py:13-18)
+
+Instead of a gRPC call into a daemon, ``tensor_dict`` runs the load in-process: each
+rank (one process per GPU, ranks joined by torch.distributed) stages its leaf-aligned
+1/N of the canonical bytes, the ranks exchange the bytes of each other's views over
+NVLink, and every rank returns its tensors as views of one device buffer.
+
+Verification follows verification_stage.cc:55-141: the data multihash of the loaded
+bytes is always computed on the GPU (leaf size from the adaptive policy of
+compute_data_multihash_from_gpu, unless ``leaf_chunk_bytes`` is given); when an
+``artifact_descriptor.json`` next to the artifact holds a data multihash, a mismatch
+raises ``ArtifactError`` with status DATA_LOSS ("ARTIFACT_ID_MISMATCH").
+"""
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native
+from .artifact import build_canonical_index, build_source_index, canonical_segments, pad_ranges, safetensors_files
+from .hashing import DEFAULT_LEAF_CHUNK_BYTES, determine_leaf_chunk_size
+from .loader import Group, read_segments, stage_bounds
+from .views import JOB_DTYPE, build_view_spec, plan_view
+
+_TORCH_DTYPES = {
+    "torch.bfloat16": torch.bfloat16, "torch.float16": torch.float16, "torch.float32": torch.float32,
+    "torch.float": torch.float32, "torch.float64": torch.float64, "torch.double": torch.float64,
+    "torch.int8": torch.int8, "torch.uint8": torch.uint8, "torch.int16": torch.int16, "torch.int32": torch.int32,
+    "torch.int64": torch.int64, "torch.bool": torch.bool, "torch.float8_e4m3fn": torch.float8_e4m3fn,
+    "torch.float8_e5m2": torch.float8_e5m2,
+}
+
+
+class ArtifactError(RuntimeError):
+    def __init__(self, message: str, status_code: str = "INTERNAL", retryable: bool = False):
+        super().__init__(message)
+        self.status_code = status_code
+        self.retryable = retryable
+
+
+@dataclass(frozen=True)
+class CollectiveLoadGroup:
+    """Explicit collective load contract for a single materialization call."""
+
+    group_id: str
+    world_size: int
+    rank: int
+
+
+@dataclass(frozen=True)
+class CallContext:
+    collective: CollectiveLoadGroup | None = None
+
+
+@dataclass(frozen=True)
+class GetArtifactOptions:
+    export_policy: str | None = None
+
+
+_GROUPS: dict = {}
+
+
+def _group_for(device_index: int, world: int, rank: int, group_id: str) -> Group:
+    key = (device_index, world, rank, group_id)
+    g = _GROUPS.get(key)
+    if g is None:
+        if world == 1:
+            g = Group(1, 0, device_index)
+        else:
+            import torch.distributed as dist
+            if not dist.is_initialized() or dist.get_world_size() != world or dist.get_rank() != rank:
+                raise ArtifactError("collective load needs torch.distributed initialised with the group's ranks",
+                                    "FAILED_PRECONDITION")
+            g = Group.from_torch_distributed(device_index)
+        _GROUPS[key] = g
+    return g
+
+
+def gather_rank_jobs(jobs: np.ndarray, world: int) -> list:
+    """Every rank's view copy jobs (all ranks call it; one all_gather of the job bytes)."""
+    if world == 1:
+        return [jobs]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, jobs.tobytes())
+    return [np.frombuffer(b, dtype=JOB_DTYPE).copy() for b in out]
+
+
+def _read_descriptor(path: str):
+    d = path if os.path.isdir(path) else os.path.dirname(path)
+    p = os.path.join(d, "artifact_descriptor.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f)
+
+
+class Artifact:
+    """A lazy handle on a safetensors artifact (optionally a subset / view of it)."""
+
+    def __init__(self, path: str, index, *, subset=None, spec=None, verify_checksums=True, leaf_chunk_bytes=None,
+                 key=None):
+        self.path, self.index, self.key = path, index, key
+        self._subset, self._spec = subset, spec
+        self._slices, self._transpose = {}, {}
+        self.verify_checksums = verify_checksums
+        self.leaf_chunk_bytes = leaf_chunk_bytes
+        self.data_multihash: str | None = None
+
+    def _derive(self, subset=None, slices=None, transpose=None) -> "Artifact":
+        a = Artifact(self.path, self.index, subset=self._subset if subset is None else subset,
+                     verify_checksums=self.verify_checksums, leaf_chunk_bytes=self.leaf_chunk_bytes, key=self.key)
+        a._slices = dict(self._slices, **(slices or {}))
+        a._transpose = dict(self._transpose, **(transpose or {}))
+        a._spec = build_view_spec(self.index, a._slices, a._transpose)
+        return a
+
+    def subset(self, names) -> "Artifact":
+        names = [str(n) for n in names]
+        for n in names:
+            if n not in self.index.entries:
+                raise ValueError(f"View subset references unknown tensor: {n}")
+        return self._derive(subset=names)
+
+    def view(self, *, slices=None, transpose=None) -> "Artifact":
+        return self._derive(slices=slices, transpose=transpose)
+
+    def describe(self) -> str:
+        return (f"Artifact({self.path}: {len(self.index.entries)} tensors, {self.index.total_bytes} bytes, "
+                f"subset={len(self._subset) if self._subset else 'all'}, view_ops={len(self._spec.tensors) if self._spec else 0})")
+
+    @property
+    def canonical_index_json(self) -> str:
+        return self.index.to_json()
+
+    def tensor_dict(self, *, device, options: GetArtifactOptions | None = None,
+                    ctx: CallContext | None = None) -> dict:
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise ArtifactError("this build materialises on CUDA devices only", "UNIMPLEMENTED")
+        dev_index = dev.index if dev.index is not None else torch.cuda.current_device()
+        coll = ctx.collective if ctx is not None else None
+        world, rank = (coll.world_size, coll.rank) if coll is not None else (1, 0)
+        if world < 1 or not (0 <= rank < world):
+            raise ArtifactError("invalid collective group (world_size, rank)", "INVALID_ARGUMENT")
+        T = self.index.total_bytes
+        L = self.leaf_chunk_bytes or determine_leaf_chunk_size(T, DEFAULT_LEAF_CHUNK_BYTES)
+        plan = plan_view(self.index, self._spec, self._subset)
+        rank_jobs = gather_rank_jobs(plan.jobs, world)
+        bounds = stage_bounds(T, L, world)
+        lo, hi = bounds[rank], bounds[rank + 1]
+        with torch.cuda.device(dev_index):
+            h_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, pin_memory=True)
+            read_segments(canonical_segments(self.index, lo, hi), h_stage.data_ptr(), threads=min(16, os.cpu_count() or 4))
+            for off, ln in pad_ranges(self.index, lo, hi):
+                h_stage[off:off + ln].zero_()
+            d_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, device=dev)
+            alias = world == 1 and plan.is_identity
+            d_view = d_stage if alias else torch.empty(max(plan.view_bytes, 1), dtype=torch.uint8, device=dev)
+            expected = None
+            desc = _read_descriptor(self.path) if self.verify_checksums else None
+            if desc and desc.get("data_multihash") and not self.leaf_chunk_bytes:
+                expected = _root_of_multihash(desc["data_multihash"])
+            group = _group_for(dev_index, world, rank, coll.group_id if coll else "")
+            try:
+                res = group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage,
+                                 permutes=plan.permutes, view_bytes=plan.view_bytes, expected_root=expected)
+            except _native.TcxError as e:
+                code = {15: "DATA_LOSS", 3: "INVALID_ARGUMENT", 4: "DEADLINE_EXCEEDED"}.get(e.code, "INTERNAL")
+                raise ArtifactError(str(e), code) from e
+        self.data_multihash = res["multihash"]
+        out = {}
+        for t in plan.tensors:
+            dt = _TORCH_DTYPES[t.dtype]
+            out[t.name] = d_view[t.offset:t.offset + t.nbytes].view(dt).view(t.shape)
+        return out
+
+
+def _root_of_multihash(mh: str) -> bytes:
+    import base64
+    if not mh.startswith("b"):
+        raise ArtifactError(f"unsupported multibase prefix in {mh!r}", "INVALID_ARGUMENT")
+    body = mh[1:].upper()
+    raw = base64.b32decode(body + "=" * ((8 - len(body) % 8) % 8))
+    if raw[:2] != b"\x12\x20" or len(raw) != 34:
+        raise ArtifactError("descriptor data_multihash is not a sha2-256 multihash", "INVALID_ARGUMENT")
+    return raw[2:]
+
+
+def from_disk(path, *, key: str | None = None, verify_checksums: bool = True, show_progress=None,
+              leaf_chunk_bytes: int | None = None) -> Artifact:
+    """A lazy artifact over one safetensors file or a directory of them."""
+    path = os.fspath(path)
+    if not os.path.exists(path):
+        raise ArtifactError(f"path does not exist: {path}", "NOT_FOUND")
+    index = build_canonical_index(build_source_index(safetensors_files(path)))
+    return Artifact(path, index, verify_checksums=verify_checksums, leaf_chunk_bytes=leaf_chunk_bytes, key=key)
