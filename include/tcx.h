@@ -127,6 +127,24 @@ tcx_status tcx_multihash_encode(const uint8_t* digest32, char* out, size_t out_c
 tcx_status tcx_multihash_from_gpu(const void* d_src, uint64_t total_bytes, int device_id, uint64_t leaf_chunk_bytes,
                                   char* out, size_t out_capacity);
 
+/* The data multihash of tcx_multihash_from_gpu, for callers that cannot call
+ * cudaMalloc at that moment: an engine that has already reserved nearly all
+ * device memory for its own pool, or a path that must not wait on cudaFree
+ * (which synchronises the device). It allocates nothing, device or host: its
+ * scratch is a fixed array in the library's device memory, held by every GPU
+ * that loads the library until the process exits. No counterpart in the
+ * reference.
+ * Same arguments, checks, leaf policy and result as tcx_multihash_from_gpu,
+ * plus the stream the work runs on (NULL: the legacy default stream); returns
+ * once the result is on the host. Limit: at most 16384 leaves per call (64 GiB
+ * at the 4 MiB default leaf); more is INVALID_ARGUMENT.
+ * The first call on a device finds the scratch array's device address; make
+ * that first call before any stream capture. Calls on one device share the
+ * scratch and are serialised by the library; work that overlaps them on the
+ * GPU from elsewhere with the same scratch would race. */
+tcx_status tcx_multihash_from_gpu_noalloc(const void* d_src, uint64_t total_bytes, int device_id,
+                                          uint64_t leaf_chunk_bytes, char* out, size_t out_capacity, void* stream);
+
 /* Load the hashing kernels and the per-device stream and buffers of device_id;
  * the caller's current device is restored. Replaces
  * prewarm_gpu_hash_nvrtc_for_device (core/common/artifact_hash_gpu.cc:830-854). */

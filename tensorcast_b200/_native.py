@@ -105,6 +105,8 @@ _SIGNATURES = {
     "tcx_merkle_root": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_void_p]),
     "tcx_multihash_encode": (_c.c_int, [_c.c_void_p, _c.c_char_p, _c.c_size_t]),
     "tcx_multihash_from_gpu": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_int, _c.c_uint64, _c.c_char_p, _c.c_size_t]),
+    "tcx_multihash_from_gpu_noalloc": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_int, _c.c_uint64, _c.c_char_p,
+                                                  _c.c_size_t, _c.c_void_p]),
     "tcx_prewarm_device": (_c.c_int, [_c.c_int]),
     "tcx_prewarm_visible_devices": (_c.c_int, []),
     "tcx_copy_jobs_scratch_bytes": (_c.c_uint64, [_c.c_uint64]),
