@@ -517,13 +517,15 @@ def measured_hbm() -> dict:
 
 def profiled_traffic(nbytes: int):
     """DRAM bytes of one launch, scaled from the committed ncu capture of the leaf kernel."""
-    p = os.path.join(ROOT, "profiles", "sha256_leaf_traffic.json")
+    p = os.path.join(ROOT, "profiles", "sha256_leaf_traffic.txt")
     try:
         with open(p) as f:
-            d = json.load(f)
-        return round(d["dram_bytes_per_hashed_byte"] * nbytes)
-    except Exception:
-        return None
+            for line in f:
+                if line.startswith("dram_bytes_per_hashed_byte:"):
+                    return round(float(line.split(":", 1)[1]) * nbytes)
+    except OSError:
+        pass
+    return None
 
 
 if __name__ == "__main__":
