@@ -100,6 +100,29 @@ tcx_status tcx_sha256_leaves_pass(const void* d_src, uint64_t total_bytes, uint6
  * one chain (32 chains). No reference counterpart (measurement aid). */
 tcx_status tcx_sha256_compute_probe(uint32_t n_chains, uint32_t blocks, void* d_out, void* stream);
 
+/* Per-leaf SHA-256 over an explicit leaf table, stream-ordered: leaf i covers
+ * d_leaf_lengths[i] bytes at d_src + d_leaf_offsets[i] (device arrays); its
+ * digest goes to d_digests + 32*i. For segmented inputs (e.g. one buffer per
+ * sequence, each split into its own leaves) and for hashing a subset of leaves
+ * (the leaf-indexed digests of verification_utils.cc:337-369). Pass
+ * offsets_aligned16 = 1 only if d_src and every offset are 16-byte aligned
+ * (vectorised kernels); 0 works for any alignment. */
+tcx_status tcx_sha256_leaf_table(const void* d_src, const uint64_t* d_leaf_offsets, const uint32_t* d_leaf_lengths,
+                                 uint64_t n_leaves, int offsets_aligned16, void* d_digests, void* stream);
+
+/* Scratch bytes tcx_merkle_roots_segmented needs (only segments of more than
+ * 2048 leaves use it). seg_first: host array of n_segments + 1 leaf indices. */
+uint64_t tcx_merkle_segments_scratch_bytes(const uint64_t* seg_first, uint64_t n_segments);
+
+/* One Merkle root per segment, stream-ordered: segment s is leaves
+ * [seg_first[s], seg_first[s+1]) of d_digests and its root (tree of
+ * compute_tree_hash_sha256, artifact_hash_cpu.cc:198-233) goes to
+ * d_roots + 32*s. seg_first is given twice: on the host (to plan) and on the
+ * device (d_seg_first, read by the kernel). Empty segments are rejected. */
+tcx_status tcx_merkle_roots_segmented(const void* d_digests, const uint64_t* seg_first, const uint64_t* d_seg_first,
+                                      uint64_t n_segments, void* d_scratch, uint64_t scratch_bytes, void* d_roots,
+                                      void* stream);
+
 /* Scratch bytes tcx_merkle_root needs for n leaf digests. */
 uint64_t tcx_merkle_scratch_bytes(uint64_t n_leaves);
 
@@ -280,6 +303,26 @@ tcx_status tcx_plan_exchange(const tcx_load_plan* plan, int world, int rank, tcx
  * parallel preads; a short read is DATA_LOSS (source_hash.cc:44-51). */
 tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n, void* dst, int threads);
 
+/* Maps [offset, offset + length) of a file read-only into host memory and, when
+ * register_pinned != 0, page-locks the mapping (cudaHostRegister, read-only)
+ * so that host-to-device copies read the file's page-cache pages directly: a
+ * tmpfs-resident artifact can be staged without a second host copy. *host_ptr
+ * is the first mapped byte; release with tcx_host_unmap_file(handle).
+ * UNAVAILABLE if the driver refuses to register the mapping. Replaces the
+ * pread-into-pinned-pool staging of collective_disk_loader.cc:4254-4261. */
+tcx_status tcx_host_map_file(const char* path, uint64_t offset, uint64_t length, int register_pinned,
+                             void** host_ptr, void** handle);
+
+/* Unregisters and unmaps a mapping made by tcx_host_map_file. */
+tcx_status tcx_host_unmap_file(void* handle);
+
+/* Binds the calling thread to the CPUs local to CUDA device `device` (sysfs
+ * local_cpulist of its PCI function), so pinned staging buffers it allocates
+ * and touches afterwards live on the GPU's NUMA node; *n_cpus_out (may be
+ * NULL) receives the CPU count. Stands in for the NUMA options of the
+ * reference's pinned pool (core/common/memory/). */
+tcx_status tcx_bind_device_cpus(int device, int* n_cpus_out);
+
 /* A new NCCL unique id (rank 0 creates it; the caller distributes the bytes). */
 tcx_status tcx_group_unique_id(uint8_t* out128);
 
@@ -311,6 +354,25 @@ typedef struct tcx_load_result {
  * (verification_stage.cc:130-141). */
 tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage, void* d_view,
                           const uint8_t* expected_root, tcx_load_result* out);
+
+/* ---------------------------------------------------------------------------
+ * Paged KV-cache gather (no reference counterpart: the reference stores
+ * engine-owned KV as opaque byte artifacts, tests/python/test_kvcache_adapter.py).
+ * ------------------------------------------------------------------------ */
+
+/* Gathers each sequence's pages from a paged pool into one contiguous buffer,
+ * stream-ordered. Pool page p of plane k: d_pool + (k*pool_pages + p) *
+ * page_tokens*token_bytes. Sequence s has d_seq_tokens[s] tokens in pages
+ * d_page_table[d_page_offsets[s] .. d_page_offsets[s+1]) and is written at
+ * d_out + d_out_offsets[s] as [plane][token][token_bytes]. total_pages =
+ * d_page_offsets[n_seq] (host copy). Table entries are checked on the device:
+ * a bad one skips that page and leaves a non-zero code in *d_status (1 slot out
+ * of the pool, 2 page past the sequence's tokens, 3 output past out_bytes);
+ * *d_status must be zero before the call. */
+tcx_status tcx_kv_gather(const void* d_pool, uint32_t planes, uint64_t pool_pages, uint32_t page_tokens,
+                         uint64_t token_bytes, const uint32_t* d_page_table, const uint64_t* d_page_offsets,
+                         const uint32_t* d_seq_tokens, const uint64_t* d_out_offsets, uint64_t n_seq,
+                         uint64_t total_pages, void* d_out, uint64_t out_bytes, uint32_t* d_status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -102,6 +102,14 @@ _SIGNATURES = {
     "tcx_sha256_leaves_pass": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_uint64, _c.c_uint64, _c.c_uint64,
                                           _c.c_void_p, _c.c_void_p, _c.c_uint64, _c.c_void_p]),
     "tcx_merkle_scratch_bytes": (_c.c_uint64, [_c.c_uint64]),
+    "tcx_sha256_leaf_table": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_uint64, _c.c_int, _c.c_void_p,
+                                         _c.c_void_p]),
+    "tcx_merkle_segments_scratch_bytes": (_c.c_uint64, [_c.c_void_p, _c.c_uint64]),
+    "tcx_merkle_roots_segmented": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_uint64, _c.c_void_p,
+                                              _c.c_uint64, _c.c_void_p, _c.c_void_p]),
+    "tcx_kv_gather": (_c.c_int, [_c.c_void_p, _c.c_uint32, _c.c_uint64, _c.c_uint32, _c.c_uint64, _c.c_void_p,
+                                 _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_uint64, _c.c_uint64, _c.c_void_p,
+                                 _c.c_uint64, _c.c_void_p, _c.c_void_p]),
     "tcx_merkle_root": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_uint64, _c.c_void_p, _c.c_void_p]),
     "tcx_multihash_encode": (_c.c_int, [_c.c_void_p, _c.c_char_p, _c.c_size_t]),
     "tcx_multihash_from_gpu": (_c.c_int, [_c.c_void_p, _c.c_uint64, _c.c_int, _c.c_uint64, _c.c_char_p, _c.c_size_t]),
@@ -116,6 +124,10 @@ _SIGNATURES = {
     "tcx_plan_exchange_capacity": (_c.c_uint64, [_c.POINTER(LoadPlan), _c.c_int]),
     "tcx_plan_exchange": (_c.c_int, [_c.POINTER(LoadPlan), _c.c_int, _c.c_int, _c.POINTER(ExchangePlan)]),
     "tcx_read_segments": (_c.c_int, [_c.POINTER(FileSegment), _c.c_uint64, _c.c_void_p, _c.c_int]),
+    "tcx_host_map_file": (_c.c_int, [_c.c_char_p, _c.c_uint64, _c.c_uint64, _c.c_int, _c.POINTER(_c.c_void_p),
+                                     _c.POINTER(_c.c_void_p)]),
+    "tcx_host_unmap_file": (_c.c_int, [_c.c_void_p]),
+    "tcx_bind_device_cpus": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_int)]),
     "tcx_group_unique_id": (_c.c_int, [_c.c_void_p]),
     "tcx_group_create": (_c.c_int, [_c.c_void_p, _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.POINTER(_c.c_void_p)]),
     "tcx_group_destroy": (_c.c_int, [_c.c_void_p]),

@@ -41,17 +41,22 @@ constexpr uint32_t kFinishMax = 2048;  // levels at or below this size finish in
 constexpr int kFinishThreads = 1024;
 
 // ---------------------------------------------------------------------------
-// Leaf kernel.
-// kVec: every leaf start is 16-byte aligned (16-aligned base, L % 16 == 0).
-// Otherwise each leaf start has a fixed misalignment s = addr & 3 and a block is
-// assembled from 17 aligned words with funnel shifts. Every word read lies in the
-// same aligned 4-byte word as at least one byte of the leaf, so no read can leave
-// the pages of the buffer.
+// Leaf geometry. Uniform: leaf i covers [i*leaf, min((i+1)*leaf, total)).
+// Table: leaf i covers [off[i], off[i] + len[i]) (segmented inputs such as
+// per-sequence buffers, or a chosen subset of leaves).
 // ---------------------------------------------------------------------------
+struct LeafGeom {
+  uint64_t total;
+  uint64_t leaf;
+  const uint64_t* off;  // table mode when non-null
+  const uint32_t* len;
+};
+
 // Per-chain quantities of one pass. A pass covers [seg_off, seg_off + seg_len) of
 // every leaf (seg_off and, unless it reaches the leaf end, seg_len are multiples
 // of 64). The chain is finalised in the pass that reaches its end.
 struct LeafPass {
+  uint64_t start;     // byte offset of the leaf in the source
   uint64_t leaf_len;  // bytes of this leaf
   uint64_t begin;     // first byte of the pass inside the leaf
   uint64_t nfull;     // full 64-byte blocks of leaf data in this pass
@@ -60,12 +65,18 @@ struct LeafPass {
   bool finalize;      // the pass reaches the leaf end: pad and emit the digest
 };
 
-__device__ __forceinline__ LeafPass leaf_pass(uint32_t i, uint32_t n_leaves, uint64_t total, uint64_t leaf,
-                                              uint64_t seg_off, uint64_t seg_len) {
+__device__ __forceinline__ LeafPass leaf_pass(uint32_t i, uint32_t n_leaves, const LeafGeom& g, uint64_t seg_off,
+                                              uint64_t seg_len) {
   LeafPass p{};
   if (i >= n_leaves) return p;
-  const uint64_t off = static_cast<uint64_t>(i) * leaf;
-  p.leaf_len = min(leaf, total - off);
+  if (g.off != nullptr) {
+    p.start = g.off[i];
+    p.leaf_len = g.len[i];
+  } else {
+    p.start = static_cast<uint64_t>(i) * g.leaf;
+    p.leaf_len = min(g.leaf, g.total - p.start);
+  }
+  if (p.leaf_len == 0) return p;
   if (seg_off >= p.leaf_len) return p;
   p.active = true;
   p.begin = seg_off;
@@ -104,15 +115,14 @@ __device__ __forceinline__ void save_state(const uint32_t s[8], uint32_t* states
 // the pages of the buffer.
 // ---------------------------------------------------------------------------
 template <bool kVec>
-__global__ void __launch_bounds__(kLeafThreads) sha256_leaf_kernel(const uint8_t* __restrict__ src, uint64_t total,
-                                                                   uint64_t leaf, uint32_t n_leaves,
-                                                                   uint64_t seg_off, uint64_t seg_len,
-                                                                   uint32_t* __restrict__ states,
+__global__ void __launch_bounds__(kLeafThreads) sha256_leaf_kernel(const uint8_t* __restrict__ src, LeafGeom geom,
+                                                                   uint32_t n_leaves, uint64_t seg_off,
+                                                                   uint64_t seg_len, uint32_t* __restrict__ states,
                                                                    uint8_t* __restrict__ digests) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  const LeafPass ps = leaf_pass(i, n_leaves, total, leaf, seg_off, seg_len);
+  const LeafPass ps = leaf_pass(i, n_leaves, geom, seg_off, seg_len);
   if (!ps.active) return;
-  const uint8_t* p = src + static_cast<uint64_t>(i) * leaf + ps.begin;
+  const uint8_t* p = src + ps.start + ps.begin;
   const uint64_t nfull = ps.nfull;
 
   uint32_t s[8];
@@ -236,7 +246,13 @@ __device__ __forceinline__ void ws_produce_block(uint4* dst, uint32_t w[16], uin
   }
 }
 
-__device__ __forceinline__ void ws_consume_block(uint32_t s[8], const uint4* src, uint32_t lane, bool keep) {
+// 64 rounds of one block from K[t]+W[t] in shared memory. The two recurrences
+// (e' = d + T1 and a' = T1 + T2) stay three-input adds on the integer ALU; the
+// adds that feed them but sit off the recurrence (h + KW, + d, T1) go to the FMA
+// pipe as multiply-adds by `one` (a kernel argument equal to 1 that the compiler
+// cannot fold), which shortens the per-round ALU queue of the single consumer warp.
+__device__ __forceinline__ void ws_consume_block(uint32_t s[8], const uint4* src, uint32_t lane, bool keep,
+                                                 uint32_t one) {
   uint32_t a = s[0], b = s[1], c = s[2], d = s[3], e = s[4], f = s[5], g = s[6], h = s[7];
 #pragma unroll
   for (int q = 0; q < 16; ++q) {
@@ -244,16 +260,20 @@ __device__ __forceinline__ void ws_consume_block(uint32_t s[8], const uint4* src
     const uint32_t kw[4] = {kw4.x, kw4.y, kw4.z, kw4.w};
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const uint32_t t1 = h + kw[r] + dev::big_sigma1(e) + dev::choose(e, f, g);
-      const uint32_t t2 = dev::big_sigma0(a) + dev::majority(a, b, c);
+      const uint32_t hk = h * one + kw[r];
+      const uint32_t hkd = hk * one + d;
+      const uint32_t s1 = dev::big_sigma1(e), ch = dev::choose(e, f, g);
+      const uint32_t ne = hkd + s1 + ch;
+      const uint32_t t1 = (s1 * one + hk) * one + ch;
+      const uint32_t na = t1 + dev::big_sigma0(a) + dev::majority(a, b, c);
       h = g;
       g = f;
       f = e;
-      e = d + t1;
+      e = ne;
       d = c;
       c = b;
       b = a;
-      a = t1 + t2;
+      a = na;
     }
   }
   if (keep) {
@@ -263,17 +283,16 @@ __device__ __forceinline__ void ws_consume_block(uint32_t s[8], const uint4* src
 }
 
 __global__ void __launch_bounds__(kWsThreads, 1) sha256_leaf_ws_kernel(const uint8_t* __restrict__ src,
-                                                                       uint64_t total, uint64_t leaf,
-                                                                       uint32_t n_leaves, uint64_t seg_off,
-                                                                       uint64_t seg_len,
+                                                                       LeafGeom geom, uint32_t n_leaves,
+                                                                       uint64_t seg_off, uint64_t seg_len,
                                                                        uint32_t* __restrict__ states,
-                                                                       uint8_t* __restrict__ digests) {
+                                                                       uint8_t* __restrict__ digests, uint32_t one) {
   extern __shared__ uint4 ws_smem[];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const bool producer = warp >= kWsPairs;
   const uint32_t pair = producer ? warp - kWsPairs : warp;
   const uint32_t i = blockIdx.x * (32u * kWsPairs) + pair * 32u + lane;
-  const LeafPass ps = leaf_pass(i, n_leaves, total, leaf, seg_off, seg_len);
+  const LeafPass ps = leaf_pass(i, n_leaves, geom, seg_off, seg_len);
   const uint32_t max_nb = __reduce_max_sync(0xffffffffu, ps.active ? ps.nb : 0u);
   const uint32_t n_stages = (max_nb + kWsBlocks - 1) / kWsBlocks;
   uint4* ring = ws_smem + static_cast<size_t>(pair) * kWsStages * (kWsStageWords / 4);
@@ -281,7 +300,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) sha256_leaf_ws_kernel(const uin
   const uint32_t bar_empty = bar_full + kWsStages;
 
   if (producer) {
-    const uint8_t* p = src + (ps.active ? static_cast<uint64_t>(i) * leaf + ps.begin : 0ull);
+    const uint8_t* p = src + (ps.active ? ps.start + ps.begin : 0ull);
     const uint4* q = reinterpret_cast<const uint4*>(p);
     uint4 cur[4], nxt[4];
     if (ps.active && ps.nfull > 0) {
@@ -331,7 +350,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) sha256_leaf_ws_kernel(const uin
 #pragma unroll 1
       for (int blk = 0; blk < kWsBlocks; ++blk, ++b) {
         if (b >= max_nb) break;
-        ws_consume_block(s, stage + blk * (kWsBlockWords / 4), lane, ps.active && b < ps.nb);
+        ws_consume_block(s, stage + blk * (kWsBlockWords / 4), lane, ps.active && b < ps.nb, one);
       }
       named_bar_arrive(bar_empty + slot, 64);
     }
@@ -441,6 +460,52 @@ __global__ void __launch_bounds__(kFinishThreads) merkle_finish_kernel(const uin
   if (threadIdx.x < 2) reinterpret_cast<uint4*>(root)[threadIdx.x] = smem4[threadIdx.x];
 }
 
+// Per-segment roots: CTA s reduces the digests of segment s (at most
+// kFinishMax leaves) in shared memory and writes its root to roots + 32*s.
+__global__ void __launch_bounds__(kFinishThreads) merkle_segments_kernel(const uint8_t* __restrict__ digests,
+                                                                         const uint64_t* __restrict__ seg_first,
+                                                                         uint8_t* __restrict__ roots) {
+  extern __shared__ uint4 seg4[];
+  const uint64_t first = seg_first[blockIdx.x];
+  uint32_t m = static_cast<uint32_t>(seg_first[blockIdx.x + 1] - first);
+  if (m == 0 || m > kFinishMax) return;  // empty segments are rejected on the host; big ones reduced separately
+  uint8_t* nodes = reinterpret_cast<uint8_t*>(seg4);
+  const uint4* s4 = reinterpret_cast<const uint4*>(digests + 32ull * first);
+  for (uint32_t k = threadIdx.x; k < 2 * m; k += blockDim.x) seg4[k] = s4[k];
+  __syncthreads();
+  while (m > 1) {
+    const uint32_t pairs = m / 2;
+    const uint32_t j = threadIdx.x;
+    uint32_t st[8];
+    uint4 keep0 = make_uint4(0, 0, 0, 0), keep1 = keep0;
+    if (j < pairs) {
+      const uint4* q = reinterpret_cast<const uint4*>(nodes + 64u * j);
+      uint32_t w[16];
+      dev::init_state(st);
+      dev::words_from_vec(w, q[0], q[1], q[2], q[3]);
+      dev::compress(st, w);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) w[k] = 0;
+      w[0] = 0x80000000u;
+      w[15] = 512u;
+      dev::compress(st, w);
+    } else if (j == pairs && (m & 1u)) {
+      keep0 = seg4[2 * (m - 1)];
+      keep1 = seg4[2 * (m - 1) + 1];
+    }
+    __syncthreads();
+    if (j < pairs) {
+      dev::store_digest(nodes + 32u * j, st);
+    } else if (j == pairs && (m & 1u)) {
+      seg4[2 * j] = keep0;
+      seg4[2 * j + 1] = keep1;
+    }
+    __syncthreads();
+    m = pairs + (m & 1u);
+  }
+  if (threadIdx.x < 2) reinterpret_cast<uint4*>(roots + 32ull * blockIdx.x)[threadIdx.x] = seg4[threadIdx.x];
+}
+
 // ---------------------------------------------------------------------------
 // Host helpers.
 // ---------------------------------------------------------------------------
@@ -468,9 +533,11 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-// Chains up to which the warp-specialised kernel is chosen (one wave of CTAs
-// with a consumer and a producer warp per SMSP pair).
-static constexpr uint32_t kWsMaxChains = 148u * 32u * kWsPairs * 2u;
+// Chains up to which the warp-specialised kernel is chosen. Measured on B200: the
+// warp-specialised kernel is ahead up to ~65k chains (per-chain latency matters
+// while chains are scarce), the one-thread-per-chain kernel above ~100k chains
+// (ALU throughput matters once every SMSP holds two or more chain warps).
+static constexpr uint32_t kWsMaxChains = 98304u;
 
 static int hash_kernel_choice() {
   // TCX_HASH_KERNEL=plain|ws|auto (default auto) selects the leaf kernel.
@@ -481,11 +548,9 @@ static int hash_kernel_choice() {
   return 0;
 }
 
-tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, uint64_t seg_off,
-                            uint64_t seg_len, uint32_t* states, void* d_digests, cudaStream_t stream) {
-  const auto* src = static_cast<const uint8_t*>(d_src);
-  auto* out = static_cast<uint8_t*>(d_digests);
-  const bool vec = aligned16(d_src) && leaf % 16 == 0;
+static tcx_status launch_leaf_kernels(const uint8_t* src, const LeafGeom& geom, uint32_t n, bool vec,
+                                      uint64_t seg_off, uint64_t seg_len, uint32_t* states, uint8_t* out,
+                                      cudaStream_t stream) {
   const int choice = hash_kernel_choice();
   const bool ws = vec && (choice == 2 || (choice == 0 && n <= kWsMaxChains));
   if (ws) {
@@ -498,21 +563,36 @@ tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, ui
       configured_device = dev;
     }
     const dim3 grid(static_cast<unsigned>(div_up(n, 32u * kWsPairs)));
-    sha256_leaf_ws_kernel<<<grid, kWsThreads, kWsSmemBytes, stream>>>(src, total, leaf, n, seg_off, seg_len,
-                                                                       states, out);
+    sha256_leaf_ws_kernel<<<grid, kWsThreads, kWsSmemBytes, stream>>>(src, geom, n, seg_off, seg_len, states, out,
+                                                                       1u);
     note_launches(1);
   } else if (vec) {
     const dim3 grid(static_cast<unsigned>(div_up(n, kLeafThreads)));
-    sha256_leaf_kernel<true><<<grid, kLeafThreads, 0, stream>>>(src, total, leaf, n, seg_off, seg_len, states, out);
+    sha256_leaf_kernel<true><<<grid, kLeafThreads, 0, stream>>>(src, geom, n, seg_off, seg_len, states, out);
     note_launches(1);
   } else {
     const dim3 grid(static_cast<unsigned>(div_up(n, kLeafThreads)));
-    sha256_leaf_kernel<false><<<grid, kLeafThreads, 0, stream>>>(src, total, leaf, n, seg_off, seg_len, states,
-                                                                 out);
+    sha256_leaf_kernel<false><<<grid, kLeafThreads, 0, stream>>>(src, geom, n, seg_off, seg_len, states, out);
     note_launches(1);
   }
   TCX_CUDA_TRY(cudaGetLastError());
   return TCX_OK;
+}
+
+tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, uint64_t seg_off,
+                            uint64_t seg_len, uint32_t* states, void* d_digests, cudaStream_t stream) {
+  const LeafGeom geom{total, leaf, nullptr, nullptr};
+  const bool vec = aligned16(d_src) && leaf % 16 == 0;
+  return launch_leaf_kernels(static_cast<const uint8_t*>(d_src), geom, n, vec, seg_off, seg_len, states,
+                             static_cast<uint8_t*>(d_digests), stream);
+}
+
+tcx_status launch_leaf_table(const void* d_src, const uint64_t* d_off, const uint32_t* d_len, uint32_t n,
+                             bool offsets_aligned16, void* d_digests, cudaStream_t stream) {
+  const LeafGeom geom{0, 0, d_off, d_len};
+  const bool vec = aligned16(d_src) && offsets_aligned16;
+  return launch_leaf_kernels(static_cast<const uint8_t*>(d_src), geom, n, vec, 0, ~0ull, nullptr,
+                             static_cast<uint8_t*>(d_digests), stream);
 }
 
 tcx_status launch_leaves(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, void* d_digests,
@@ -798,6 +878,60 @@ extern "C" tcx_status tcx_prewarm_visible_devices(void) {
       const std::string msg = tcx_last_error();
       return set_errorf(st, "GPU hash prewarm failed for device %d: %s", d, msg.c_str());
     }
+  }
+  return TCX_OK;
+}
+
+extern "C" tcx_status tcx_sha256_leaf_table(const void* d_src, const uint64_t* d_leaf_offsets,
+                                            const uint32_t* d_leaf_lengths, uint64_t n_leaves, int offsets_aligned16,
+                                            void* d_digests, void* stream) {
+  if (n_leaves == 0) return set_error(TCX_INVALID_ARGUMENT, "Leaf digests must not be empty");
+  if (n_leaves > 0xffffffffull) return set_error(TCX_INVALID_ARGUMENT, "Leaf count exceeds supported range");
+  if (d_src == nullptr || d_leaf_offsets == nullptr || d_leaf_lengths == nullptr || d_digests == nullptr)
+    return set_error(TCX_INVALID_ARGUMENT, "null device pointer");
+  if (!aligned16(d_digests)) return set_error(TCX_INVALID_ARGUMENT, "digest buffer must be 16-byte aligned");
+  return launch_leaf_table(d_src, d_leaf_offsets, d_leaf_lengths, static_cast<uint32_t>(n_leaves),
+                           offsets_aligned16 != 0, d_digests, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" uint64_t tcx_merkle_segments_scratch_bytes(const uint64_t* seg_first, uint64_t n_segments) {
+  uint64_t need = 256;
+  for (uint64_t s = 0; s < n_segments; ++s) {
+    const uint64_t m = seg_first[s + 1] - seg_first[s];
+    if (m > kFinishMax) need = std::max(need, merkle_scratch_bytes(m));
+  }
+  return need;
+}
+
+extern "C" tcx_status tcx_merkle_roots_segmented(const void* d_digests, const uint64_t* seg_first,
+                                                 const uint64_t* d_seg_first, uint64_t n_segments, void* d_scratch,
+                                                 uint64_t scratch_bytes, void* d_roots, void* stream) {
+  if (n_segments == 0) return TCX_OK;
+  if (d_digests == nullptr || seg_first == nullptr || d_seg_first == nullptr || d_roots == nullptr)
+    return set_error(TCX_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(d_digests) || !aligned16(d_roots))
+    return set_error(TCX_INVALID_ARGUMENT, "digests and roots must be 16-byte aligned");
+  if (n_segments > 0x7fffffffull) return set_error(TCX_INVALID_ARGUMENT, "too many segments");
+  for (uint64_t s = 0; s < n_segments; ++s) {
+    if (seg_first[s + 1] <= seg_first[s]) return set_errorf(TCX_INVALID_ARGUMENT, "segment %llu has no leaves",
+                                                             static_cast<unsigned long long>(s));
+  }
+  if (scratch_bytes < tcx_merkle_segments_scratch_bytes(seg_first, n_segments) ||
+      (d_scratch != nullptr && !aligned16(d_scratch)))
+    return set_error(TCX_INVALID_ARGUMENT, "segment Merkle scratch too small or misaligned");
+  const auto st = static_cast<cudaStream_t>(stream);
+  TCX_CUDA_TRY(cudaFuncSetAttribute(merkle_segments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kFinishMax * 32)));
+  merkle_segments_kernel<<<static_cast<unsigned>(n_segments), kFinishThreads, kFinishMax * 32, st>>>(
+      static_cast<const uint8_t*>(d_digests), d_seg_first, static_cast<uint8_t*>(d_roots));
+  note_launches(1);
+  TCX_CUDA_TRY(cudaGetLastError());
+  for (uint64_t s = 0; s < n_segments; ++s) {
+    const uint64_t m = seg_first[s + 1] - seg_first[s];
+    if (m <= kFinishMax) continue;
+    tcx_status rc = launch_merkle(static_cast<const uint8_t*>(d_digests) + 32 * seg_first[s], m,
+                                  static_cast<uint8_t*>(d_scratch), static_cast<uint8_t*>(d_roots) + 32 * s, st);
+    if (rc != TCX_OK) return rc;
   }
   return TCX_OK;
 }

@@ -18,10 +18,14 @@
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <nccl.h>
+#include <sched.h>
+#include <sys/mman.h>
 #include <unistd.h>
 
 #include <algorithm>
 #include <atomic>
+#include <cctype>
+#include <cstdio>
 #include <chrono>
 #include <cstring>
 #include <thread>
@@ -496,5 +500,98 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   out->total_ms = elapsed_ms(g->ev_start, g->ev_end);
   if (expected_root != nullptr && std::memcmp(expected_root, out->root, 32) != 0)
     return set_error(TCX_DATA_LOSS, "ARTIFACT_ID_MISMATCH: data multihash of the loaded bytes differs from the expected one");
+  return TCX_OK;
+}
+
+namespace {
+struct FileMapping {
+  void* base = nullptr;
+  uint64_t length = 0;
+  bool registered = false;
+};
+}  // namespace
+
+extern "C" tcx_status tcx_host_map_file(const char* path, uint64_t offset, uint64_t length, int register_pinned,
+                                        void** host_ptr, void** handle) {
+  if (path == nullptr || host_ptr == nullptr || handle == nullptr)
+    return set_error(TCX_INVALID_ARGUMENT, "path, host_ptr and handle are required");
+  *host_ptr = nullptr;
+  *handle = nullptr;
+  if (length == 0) return set_error(TCX_INVALID_ARGUMENT, "length must be > 0");
+  const long page = sysconf(_SC_PAGESIZE);
+  const uint64_t aligned_off = offset - offset % static_cast<uint64_t>(page);
+  const uint64_t map_len = length + (offset - aligned_off);
+  const int fd = open(path, O_RDONLY | O_CLOEXEC);
+  if (fd < 0) return set_errorf(TCX_NOT_FOUND, "open failed: %s", path);
+  off_t size = lseek(fd, 0, SEEK_END);
+  if (size < 0 || static_cast<uint64_t>(size) < offset + length) {
+    close(fd);
+    return set_errorf(TCX_OUT_OF_RANGE, "%s is shorter than the mapped range", path);
+  }
+  void* base = mmap(nullptr, map_len, PROT_READ, MAP_SHARED | MAP_POPULATE, fd, static_cast<off_t>(aligned_off));
+  close(fd);
+  if (base == MAP_FAILED) return set_errorf(TCX_RESOURCE_EXHAUSTED, "mmap of %llu bytes failed",
+                                            static_cast<unsigned long long>(map_len));
+  auto* m = new FileMapping{base, map_len, false};
+  if (register_pinned) {
+    cudaError_t e = cudaHostRegister(base, map_len, cudaHostRegisterReadOnly | cudaHostRegisterPortable);
+    if (e != cudaSuccess) {
+      munmap(base, map_len);
+      delete m;
+      return set_error(TCX_UNAVAILABLE, "cudaHostRegister of the file mapping failed: " + cuda_msg(e));
+    }
+    m->registered = true;
+  }
+  *host_ptr = static_cast<uint8_t*>(base) + (offset - aligned_off);
+  *handle = m;
+  return TCX_OK;
+}
+
+extern "C" tcx_status tcx_host_unmap_file(void* handle) {
+  if (handle == nullptr) return TCX_OK;
+  auto* m = static_cast<FileMapping*>(handle);
+  tcx_status st = TCX_OK;
+  if (m->registered) {
+    cudaError_t e = cudaHostUnregister(m->base);
+    if (e != cudaSuccess) st = set_error(TCX_INTERNAL, "cudaHostUnregister failed: " + cuda_msg(e));
+  }
+  munmap(m->base, m->length);
+  delete m;
+  return st;
+}
+
+extern "C" tcx_status tcx_bind_device_cpus(int device, int* n_cpus_out) {
+  // The CPUs on the GPU's side of the PCIe hierarchy (sysfs local_cpulist). Binding
+  // the calling thread there before it allocates pinned buffers places them, by
+  // first touch, on the GPU's NUMA node; threads it starts afterwards inherit it.
+  char bus[64] = {0};
+  TCX_CUDA_TRY(cudaDeviceGetPCIBusId(bus, sizeof bus, device));
+  for (char* c = bus; *c; ++c) *c = static_cast<char>(tolower(*c));
+  const std::string path = std::string("/sys/bus/pci/devices/") + bus + "/local_cpulist";
+  FILE* f = fopen(path.c_str(), "r");
+  if (f == nullptr) return set_errorf(TCX_NOT_FOUND, "cannot read %s", path.c_str());
+  char list[4096] = {0};
+  const size_t got = fread(list, 1, sizeof list - 1, f);
+  fclose(f);
+  list[got] = 0;
+  cpu_set_t set;
+  CPU_ZERO(&set);
+  int count = 0;
+  for (char* tok = strtok(list, ",\n"); tok != nullptr; tok = strtok(nullptr, ",\n")) {
+    int a = -1, b = -1;
+    if (sscanf(tok, "%d-%d", &a, &b) == 2) {
+    } else if (sscanf(tok, "%d", &a) == 1) {
+      b = a;
+    } else {
+      continue;
+    }
+    for (int c = a; c <= b && c < CPU_SETSIZE; ++c) {
+      CPU_SET(c, &set);
+      ++count;
+    }
+  }
+  if (count == 0) return set_errorf(TCX_NOT_FOUND, "no CPUs listed in %s", path.c_str());
+  if (sched_setaffinity(0, sizeof set, &set) != 0) return set_error(TCX_INTERNAL, "sched_setaffinity failed");
+  if (n_cpus_out) *n_cpus_out = count;
   return TCX_OK;
 }

@@ -88,6 +88,39 @@ def read_segments(segments, dst_ptr: int, threads: int = 8) -> None:
     _native.call("tcx_read_segments", arr, len(segments), dst_ptr, int(threads))
 
 
+def bind_device_cpus(device: int) -> int:
+    """Binds the calling thread (and threads it starts later) to the CPUs local to `device`;
+    returns how many. Call before allocating pinned staging buffers."""
+    n = ctypes.c_int(0)
+    _native.call("tcx_bind_device_cpus", int(device), ctypes.byref(n))
+    return n.value
+
+
+class FileMapping:
+    """A read-only mapping of a file range, page-locked for direct H2D (tcx_host_map_file)."""
+
+    def __init__(self, path: str, offset: int, length: int, register: bool = True):
+        self._h = ctypes.c_void_p()
+        ptr = ctypes.c_void_p()
+        _native.call("tcx_host_map_file", os.fsencode(path), int(offset), int(length), int(register),
+                     ctypes.byref(ptr), ctypes.byref(self._h))
+        self.ptr, self.length = int(ptr.value), int(length)
+
+    def data_ptr(self) -> int:
+        return self.ptr
+
+    def close(self) -> None:
+        if self._h:
+            _native.call("tcx_host_unmap_file", self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Group:
     """One rank of a collective load (tcx_group)."""
 
@@ -131,7 +164,7 @@ class Group:
             if len(expected_root) != 32:
                 raise ValueError("expected_root must be 32 bytes")
             exp = ctypes.create_string_buffer(bytes(expected_root), 32)
-        ptr = lambda x: None if x is None else (x.data_ptr() if isinstance(x, torch.Tensor) else int(x))  # noqa: E731
+        ptr = lambda x: None if x is None else (x.data_ptr() if hasattr(x, "data_ptr") else int(x))  # noqa: E731
         _native.call("tcx_group_load", self._h, ctypes.byref(plan.c), ptr(h_stage), ptr(d_stage), ptr(d_view), exp,
                      ctypes.byref(res))
         return {"root": bytes(res.root), "multihash": res.multihash.decode(), "leaves": res.leaves,
