@@ -494,13 +494,11 @@ def run_kv(args) -> None:
     pools, runners = [], []
     for k, sh in zip(range(rank, 8, world), shards):
         pools.append(kvcache.make_pool(sh, seed=3 * 100 + k))
+    # one output buffer per rank, reused by its shards one after another
     out_max = max(kvcache.plan(sh).out_bytes for sh in shards)
-    for sh in shards:
-        runners.append(kvcache.KvGatherHash(sh))
-    # one output buffer per rank: share the largest among the shard runners
     shared = torch.empty(out_max, dtype=torch.uint8, device="cuda")
-    for r in runners:
-        r.out = shared[: r.p.out_bytes]
+    for sh in shards:
+        runners.append(kvcache.KvGatherHash(sh, out=shared))
     torch.cuda.synchronize()
 
     def step():

@@ -303,9 +303,11 @@ tcx_status tcx_plan_exchange(const tcx_load_plan* plan, int world, int rank, tcx
  * parallel preads; a short read is DATA_LOSS (source_hash.cc:44-51). */
 tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n, void* dst, int threads);
 
-/* Maps [offset, offset + length) of a file read-only into host memory and, when
- * register_pinned != 0, page-locks the mapping (cudaHostRegister, read-only)
- * so that host-to-device copies read the file's page-cache pages directly: a
+/* Maps [offset, offset + length) of a file into host memory and, when
+ * register_pinned != 0, page-locks the mapping (cudaHostRegister; a read-only
+ * mapping registered read-only where the driver accepts it, else a shared
+ * read-write mapping that is never written) so that host-to-device copies
+ * read the file's page-cache pages directly: a
  * tmpfs-resident artifact can be staged without a second host copy. *host_ptr
  * is the first mapped byte; release with tcx_host_unmap_file(handle).
  * UNAVAILABLE if the driver refuses to register the mapping. Replaces the

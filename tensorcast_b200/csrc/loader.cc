@@ -521,27 +521,43 @@ extern "C" tcx_status tcx_host_map_file(const char* path, uint64_t offset, uint6
   const long page = sysconf(_SC_PAGESIZE);
   const uint64_t aligned_off = offset - offset % static_cast<uint64_t>(page);
   const uint64_t map_len = length + (offset - aligned_off);
-  const int fd = open(path, O_RDONLY | O_CLOEXEC);
-  if (fd < 0) return set_errorf(TCX_NOT_FOUND, "open failed: %s", path);
-  off_t size = lseek(fd, 0, SEEK_END);
-  if (size < 0 || static_cast<uint64_t>(size) < offset + length) {
-    close(fd);
-    return set_errorf(TCX_OUT_OF_RANGE, "%s is shorter than the mapped range", path);
-  }
-  void* base = mmap(nullptr, map_len, PROT_READ, MAP_SHARED | MAP_POPULATE, fd, static_cast<off_t>(aligned_off));
-  close(fd);
-  if (base == MAP_FAILED) return set_errorf(TCX_RESOURCE_EXHAUSTED, "mmap of %llu bytes failed",
-                                            static_cast<unsigned long long>(map_len));
-  auto* m = new FileMapping{base, map_len, false};
-  if (register_pinned) {
-    cudaError_t e = cudaHostRegister(base, map_len, cudaHostRegisterReadOnly | cudaHostRegisterPortable);
-    if (e != cudaSuccess) {
-      munmap(base, map_len);
-      delete m;
-      return set_error(TCX_UNAVAILABLE, "cudaHostRegister of the file mapping failed: " + cuda_msg(e));
+  // Read-only mapping registered read-only first; where the driver refuses that, a
+  // shared read-write mapping (never written) registered normally.
+  void* base = MAP_FAILED;
+  bool registered = false;
+  std::string why;
+  for (int attempt = 0; attempt < (register_pinned ? 2 : 1) && !registered; ++attempt) {
+    const bool rw = attempt == 1;
+    const int fd = open(path, (rw ? O_RDWR : O_RDONLY) | O_CLOEXEC);
+    if (fd < 0) {
+      if (attempt == 0) return set_errorf(TCX_NOT_FOUND, "open failed: %s", path);
+      break;
     }
-    m->registered = true;
+    const off_t size = lseek(fd, 0, SEEK_END);
+    if (size < 0 || static_cast<uint64_t>(size) < offset + length) {
+      close(fd);
+      return set_errorf(TCX_OUT_OF_RANGE, "%s is shorter than the mapped range", path);
+    }
+    base = mmap(nullptr, map_len, rw ? (PROT_READ | PROT_WRITE) : PROT_READ, MAP_SHARED | MAP_POPULATE, fd,
+                static_cast<off_t>(aligned_off));
+    close(fd);
+    if (base == MAP_FAILED)
+      return set_errorf(TCX_RESOURCE_EXHAUSTED, "mmap of %llu bytes failed", static_cast<unsigned long long>(map_len));
+    if (!register_pinned) break;
+    const cudaError_t e =
+        cudaHostRegister(base, map_len, rw ? cudaHostRegisterPortable : (cudaHostRegisterReadOnly | cudaHostRegisterPortable));
+    if (e == cudaSuccess) {
+      registered = true;
+    } else {
+      why += (why.empty() ? "" : "; ") + cuda_msg(e);
+      cudaGetLastError();
+      munmap(base, map_len);
+      base = MAP_FAILED;
+    }
   }
+  if (register_pinned && !registered)
+    return set_error(TCX_UNAVAILABLE, "cudaHostRegister of the file mapping failed: " + why);
+  auto* m = new FileMapping{base, map_len, registered};
   *host_ptr = static_cast<uint8_t*>(base) + (offset - aligned_off);
   *handle = m;
   return TCX_OK;

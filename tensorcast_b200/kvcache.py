@@ -131,7 +131,7 @@ def plan(w: KvWorkload, leaf: int = KV_LEAF, align: int = 256) -> KvPlan:
 class KvGatherHash:
     """Device-resident tables for one workload shard; ``run`` gathers and hashes."""
 
-    def __init__(self, w: KvWorkload, leaf: int = KV_LEAF, device="cuda"):
+    def __init__(self, w: KvWorkload, leaf: int = KV_LEAF, device="cuda", out: torch.Tensor | None = None):
         self.w, self.leaf = w, leaf
         self.p = plan(w, leaf)
         d = torch.device(device)
@@ -143,7 +143,10 @@ class KvGatherHash:
         self.leaf_off = t(self.p.leaf_offsets.view(np.int64))
         self.leaf_len = t(self.p.leaf_lengths.view(np.int32))
         self.seg_first_dev = t(self.p.seg_first.view(np.int64))
-        self.out = torch.empty(self.p.out_bytes, dtype=torch.uint8, device=d)
+        if out is not None and out.numel() < self.p.out_bytes:
+            raise ValueError("output buffer too small for the workload")
+        self.out = out[: self.p.out_bytes] if out is not None else torch.empty(self.p.out_bytes, dtype=torch.uint8,
+                                                                                device=d)
         n = max(len(self.p.leaf_lengths), 1)
         self.digests = torch.empty((n, 32), dtype=torch.uint8, device=d)
         self.roots = torch.empty((max(w.n_seq, 1), 32), dtype=torch.uint8, device=d)

@@ -137,3 +137,31 @@ def test_load_detects_corruption(cuda_device):
         assert res["root"] == expected
     finally:
         g.close()
+
+
+def test_load_from_registered_file_mapping(cuda_device, tmp_path):
+    """Staging straight from a file's page-cache pages (tcx_host_map_file) gives the same root."""
+    from tensorcast_b200.loader import FileMapping
+    canon, meta = oviews.canonical_bytes(random_tensors(9, n=30))
+    index = index_from_meta(meta, canon.size)
+    plan = plan_view(index)
+    path = tmp_path / "blob.bin"
+    head = 4096 + 123  # the staged range starts at an unaligned file offset
+    with open(path, "wb") as f:
+        f.write(b"\0" * head)
+        f.write(canon.tobytes())
+    try:
+        m = FileMapping(str(path), head, canon.size, register=True)
+    except _native.TcxError as e:
+        pytest.skip(f"driver does not register file mappings here: {e}")
+    g = Group(1, 0, 0)
+    try:
+        d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+        expected = oracle.tree_root(oracle.leaf_digests(canon, 256))
+        res = g.load(canon.size, 256, [0, canon.size], [plan.jobs], d_stage=d_stage, d_view=d_stage, h_stage=m,
+                     view_bytes=plan.view_bytes, expected_root=expected)
+        assert res["root"] == expected
+        assert (d_stage.cpu().numpy() == canon).all()
+    finally:
+        g.close()
+        m.close()
