@@ -266,6 +266,8 @@ typedef struct tcx_load_plan {
   uint64_t n_permutes;
   uint64_t view_bytes;           /* bytes of this rank's view buffer */
   uint64_t slab_bytes;           /* bytes per leaf per H2D/hash slab (0: 256 KiB) */
+  uint64_t window_bytes;         /* bytes per peer per exchange round; bounds the send/receive
+                                    scratch to about 2*(N-1) windows (0: 512 MiB) */
 } tcx_load_plan;
 
 /* Per-peer sizes and job lists of the exchange for one rank (host-only planning).

@@ -35,6 +35,7 @@
 
 namespace tcx {
 tcx_status validate_load_plan(const tcx_load_plan* plan, int world);
+void clip_jobs(const tcx_copy_job* jobs, uint64_t n, uint64_t lo, uint64_t hi, std::vector<tcx_copy_job>& out);
 }
 
 namespace {
@@ -43,6 +44,7 @@ using namespace tcx;
 using Clock = std::chrono::steady_clock;
 
 constexpr uint64_t kDefaultSlab = 256 * 1024;
+constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchange round
 
 std::string nccl_msg(ncclResult_t r) { return std::string(ncclGetErrorString(r)); }
 
@@ -76,13 +78,13 @@ struct tcx_group {
   int world = 1, rank = 0, device = 0;
   int64_t timeout_ms = 60000;
   ncclComm_t comm = nullptr;
-  cudaStream_t s_copy = nullptr, s_hash = nullptr, s_comm = nullptr;
+  cudaStream_t s_copy = nullptr, s_hash = nullptr, s_comm = nullptr, s_pack = nullptr;
   DevBuf digests_mine, states, digests_all, digests_compact, merkle_scratch, root, send, recv, perm_scratch, jobs,
       prefix;
   uint8_t* h_root = nullptr;
   tcx_copy_job* h_jobs = nullptr;
   uint64_t h_jobs_cap = 0;
-  std::vector<cudaEvent_t> slab_events;
+  std::vector<cudaEvent_t> slab_events, packed_events, sent_events;
   cudaEvent_t ev_start = nullptr, ev_h2d = nullptr, ev_hash = nullptr, ev_exch = nullptr, ev_end = nullptr;
 };
 
@@ -137,6 +139,21 @@ tcx_status wait_event(tcx_group* g, cudaEvent_t ev, Clock::time_point deadline) 
   }
 }
 
+tcx_status ensure_events(std::vector<cudaEvent_t>& v, uint64_t n) {
+  while (v.size() < n) {
+    cudaEvent_t e;
+    TCX_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    v.push_back(e);
+  }
+  return TCX_OK;
+}
+
+tcx_copy_job swap_ends(tcx_copy_job j) {
+  std::swap(j.src_off, j.dst_off);
+  std::swap(j.src_pitch, j.dst_pitch);
+  return j;
+}
+
 float elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
   float ms = 0;
   if (cudaEventElapsedTime(&ms, a, b) != cudaSuccess) return -1.f;
@@ -174,7 +191,8 @@ extern "C" tcx_status tcx_group_create(const uint8_t* unique_id, int world, int 
   };
   if (cudaStreamCreateWithFlags(&g->s_copy, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&g->s_hash, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&g->s_comm, cudaStreamNonBlocking) != cudaSuccess)
+      cudaStreamCreateWithFlags(&g->s_comm, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&g->s_pack, cudaStreamNonBlocking) != cudaSuccess)
     return fail(set_error(TCX_INTERNAL, "stream creation failed"));
   for (cudaEvent_t* ev : {&g->ev_start, &g->ev_h2d, &g->ev_hash, &g->ev_exch, &g->ev_end})
     if (cudaEventCreate(ev) != cudaSuccess) return fail(set_error(TCX_INTERNAL, "event creation failed"));
@@ -198,7 +216,7 @@ extern "C" tcx_status tcx_group_create(const uint8_t* unique_id, int world, int 
 extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   if (g == nullptr) return TCX_OK;
   cudaSetDevice(g->device);
-  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm})
+  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm, g->s_pack})
     if (s) cudaStreamSynchronize(s);
   if (g->comm) {
     ncclCommFinalize(g->comm);
@@ -211,10 +229,11 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
     b->release();
   if (g->h_root) cudaFreeHost(g->h_root);
   if (g->h_jobs) cudaFreeHost(g->h_jobs);
-  for (cudaEvent_t e : g->slab_events) cudaEventDestroy(e);
+  for (auto* v : {&g->slab_events, &g->packed_events, &g->sent_events})
+    for (cudaEvent_t e : *v) cudaEventDestroy(e);
   for (cudaEvent_t e : {g->ev_start, g->ev_h2d, g->ev_hash, g->ev_exch, g->ev_end})
     if (e) cudaEventDestroy(e);
-  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm})
+  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm, g->s_pack})
     if (s) cudaStreamDestroy(s);
   delete g;
   return TCX_OK;
@@ -341,21 +360,78 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     perm_bytes = std::max(perm_bytes, bytes);
   }
 
+  // --- exchange rounds ------------------------------------------------------
+  // Each (sender, receiver) pair's bytes form one stream of send_off/recv_counts
+  // bytes, moved in rounds of at most W bytes. Both sides cut the stream at the
+  // same offsets, so round k of a pair is in round k on both ranks.
+  uint64_t W = plan->window_bytes ? plan->window_bytes : kDefaultWindow;
+  W = std::max<uint64_t>(256, W - W % 256);
+  std::vector<int> peers;
+  for (int p = 0; p < world; ++p)
+    if (p != rank) peers.push_back(p);
+  uint64_t rounds = 0, max_send = 0, max_recv_buf = 0;
+  for (int p : peers) {
+    const uint64_t sp = send_off[p + 1] - send_off[p];
+    rounds = std::max(rounds, (sp + W - 1) / W);
+    rounds = std::max(rounds, (recv_counts[p] + W - 1) / W);
+    max_send = std::max(max_send, sp);
+    if (!direct[p]) max_recv_buf = std::max(max_recv_buf, recv_counts[p]);
+  }
+  const uint64_t send_slot = std::min(W, std::max<uint64_t>(max_send, 1));
+  const uint64_t recv_slot = std::min(W, std::max<uint64_t>(max_recv_buf, 1));
+  std::vector<uint64_t> pack_off(rounds + 1, 0), scat_off(rounds + 1, 0);
+  std::vector<tcx_copy_job> round_pack, round_scatter, tmp;
+  for (uint64_t k = 0; k < rounds; ++k) {
+    const uint64_t buf = k % 2;
+    for (size_t si = 0; si < peers.size(); ++si) {
+      const int p = peers[si];
+      const uint64_t sp = send_off[p + 1] - send_off[p];
+      if (k * W < sp) {
+        const uint64_t lo_w = send_off[p] + k * W, hi_w = send_off[p] + std::min(sp, (k + 1) * W);
+        tmp.clear();
+        for (uint64_t i = 0; i < xp.n_pack; ++i) {
+          if (pack[i].dst_off >= hi_w || pack[i].dst_off + pack[i].rows * pack[i].row_bytes <= lo_w) continue;
+          const tcx_copy_job sw = swap_ends(pack[i]);
+          clip_jobs(&sw, 1, lo_w, hi_w, tmp);
+        }
+        for (auto& j : tmp) {
+          tcx_copy_job r = swap_ends(j);
+          r.dst_off = r.dst_off - lo_w + (buf * peers.size() + si) * send_slot;
+          round_pack.push_back(r);
+        }
+      }
+      if (!direct[p] && k * W < recv_counts[p]) {
+        const uint64_t lo_w = recv_off[p] + k * W, hi_w = recv_off[p] + std::min(recv_counts[p], (k + 1) * W);
+        tmp.clear();
+        clip_jobs(scatter.data(), xp.n_scatter, lo_w, hi_w, tmp);
+        for (auto& j : tmp) {
+          j.src_off = j.src_off - lo_w + (buf * peers.size() + si) * recv_slot;
+          round_scatter.push_back(j);
+        }
+      }
+    }
+    pack_off[k + 1] = round_pack.size();
+    scat_off[k + 1] = round_scatter.size();
+  }
+
   // --- buffers --------------------------------------------------------------
-  const uint64_t n_jobs_all = xp.n_pack + local_kept.size() + xp.n_scatter + compact.size();
+  const uint64_t n_jobs_all = round_pack.size() + local_kept.size() + round_scatter.size() + compact.size();
+  const uint64_t n_launches = 2 * rounds + 2;
   if ((st = g->digests_mine.grow(std::max<uint64_t>(max_n, 1) * 32)) != TCX_OK) return st;
   if ((st = g->states.grow(std::max<uint64_t>(n_mine, 1) * 32)) != TCX_OK) return st;
   if ((st = g->merkle_scratch.grow(merkle_scratch_bytes(n_total))) != TCX_OK) return st;
   if ((st = g->root.grow(256)) != TCX_OK) return st;
   if ((st = g->jobs.grow(std::max<uint64_t>(n_jobs_all, 1) * sizeof(tcx_copy_job))) != TCX_OK) return st;
-  if ((st = g->prefix.grow((std::max<uint64_t>(n_jobs_all, 1) + 1) * 8)) != TCX_OK) return st;
-  if (send_off[world] && (st = g->send.grow(send_off[world])) != TCX_OK) return st;
-  if (recv_off[world] && (st = g->recv.grow(recv_off[world])) != TCX_OK) return st;
+  if ((st = g->prefix.grow((n_jobs_all + n_launches + 1) * 8)) != TCX_OK) return st;
+  if (rounds && max_send && (st = g->send.grow(2 * peers.size() * send_slot)) != TCX_OK) return st;
+  if (rounds && max_recv_buf && (st = g->recv.grow(2 * peers.size() * recv_slot)) != TCX_OK) return st;
   if (perm_bytes && (st = g->perm_scratch.grow(perm_bytes)) != TCX_OK) return st;
   if (world > 1) {
     if ((st = g->digests_all.grow(static_cast<uint64_t>(world) * max_n * 32)) != TCX_OK) return st;
     if ((st = g->digests_compact.grow(n_total * 32)) != TCX_OK) return st;
   }
+  if ((st = ensure_events(g->packed_events, rounds)) != TCX_OK) return st;
+  if ((st = ensure_events(g->sent_events, rounds)) != TCX_OK) return st;
   if (n_jobs_all > g->h_jobs_cap) {
     if (g->h_jobs) cudaFreeHost(g->h_jobs);
     g->h_jobs = nullptr;
@@ -364,14 +440,17 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     g->h_jobs_cap = n_jobs_all;
   }
   tcx_copy_job* hj = g->h_jobs;
-  const uint64_t o_pack = 0, o_local = xp.n_pack, o_scatter = o_local + local_kept.size(),
-                 o_compact = o_scatter + xp.n_scatter;
-  std::copy(pack.begin(), pack.begin() + xp.n_pack, hj + o_pack);
+  const uint64_t o_pack = 0, o_local = round_pack.size(), o_scatter = o_local + local_kept.size(),
+                 o_compact = o_scatter + round_scatter.size();
+  std::copy(round_pack.begin(), round_pack.end(), hj + o_pack);
   std::copy(local_kept.begin(), local_kept.end(), hj + o_local);
-  std::copy(scatter.begin(), scatter.begin() + xp.n_scatter, hj + o_scatter);
+  std::copy(round_scatter.begin(), round_scatter.end(), hj + o_scatter);
   std::copy(compact.begin(), compact.end(), hj + o_compact);
   auto* dj = static_cast<tcx_copy_job*>(g->jobs.p);
   auto* dprefix = static_cast<uint64_t*>(g->prefix.p);
+  uint64_t launch_idx = 0;
+  // Each copy-job launch gets its own prefix region (launches run on two streams).
+  auto prefix_for = [&](uint64_t job_off) { return dprefix + job_off + (launch_idx++); };
   auto* view = static_cast<uint8_t*>(d_view);
   auto* stage = static_cast<uint8_t*>(d_stage);
   const auto* hstage = static_cast<const uint8_t*>(h_stage);
@@ -390,11 +469,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
       const uint64_t n_full = mine / L, tail = mine - n_full * L;
       const uint64_t span = n_full > 0 ? L : tail;  // bytes per leaf to cover
       const uint64_t J = (span + S - 1) / S;
-      while (g->slab_events.size() < J) {
-        cudaEvent_t e;
-        TCX_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        g->slab_events.push_back(e);
-      }
+      if ((st = ensure_events(g->slab_events, J)) != TCX_OK) return st;
       for (uint64_t j = 0; j < J; ++j) {
         const uint64_t off = j * S;
         if (n_full > 0 && off < L) {
@@ -426,35 +501,48 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, alias ? g->ev_hash : g->ev_h2d, 0));
   if (n_jobs_all > 0)
     TCX_CUDA_TRY(cudaMemcpyAsync(dj, hj, n_jobs_all * sizeof(tcx_copy_job), cudaMemcpyHostToDevice, g->s_comm));
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_exch, g->s_comm));  // job tables uploaded, staged bytes complete
+  TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->ev_exch, 0));
   for (uint64_t k = 0; k < xp.n_gaps; ++k)
     TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
-  if (xp.n_pack && (st = launch_copy_jobs(stage, g->send.p, dj + o_pack, xp.n_pack, dprefix, g->s_comm)) != TCX_OK)
-    return st;
   if (!local_kept.empty() &&
-      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), dprefix, g->s_comm)) != TCX_OK)
+      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(o_local), g->s_comm)) != TCX_OK)
     return st;
   uint64_t sent = 0, received = 0;
-  if (world > 1) {
+  for (uint64_t k = 0; k < rounds; ++k) {
+    const uint64_t buf = k % 2;
+    // pack round k on the pack stream once round k-2 (same buffer) has been sent
+    if (k >= 2) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->sent_events[k - 2], 0));
+    const uint64_t np = pack_off[k + 1] - pack_off[k];
+    if (np && (st = launch_copy_jobs(stage, g->send.p, dj + o_pack + pack_off[k], np,
+                                     prefix_for(o_pack + pack_off[k]), g->s_pack)) != TCX_OK)
+      return st;
+    TCX_CUDA_TRY(cudaEventRecord(g->packed_events[k], g->s_pack));
+    TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[k], 0));
     if ((st = nccl_check(g, ncclGroupStart(), deadline, "ncclGroupStart")) != TCX_OK) return st;
-    for (int p = 0; p < world; ++p) {
-      if (p == rank) continue;
-      const uint64_t scount = send_off[p + 1] - send_off[p];
-      if (scount) {
-        st = nccl_check(g, ncclSend(g->send.bytes() + send_off[p], scount, ncclUint8, p, g->comm, g->s_comm), deadline,
-                        "ncclSend");
+    for (size_t si = 0; si < peers.size(); ++si) {
+      const int p = peers[si];
+      const uint64_t sp = send_off[p + 1] - send_off[p];
+      if (k * W < sp) {
+        const uint64_t n = std::min(W, sp - k * W);
+        st = nccl_check(g, ncclSend(g->send.bytes() + (buf * peers.size() + si) * send_slot, n, ncclUint8, p, g->comm,
+                                    g->s_comm), deadline, "ncclSend");
         if (st != TCX_OK) return st;
-        sent += scount;
+        sent += n;
       }
-      if (recv_counts[p]) {
-        uint8_t* dst = direct[p] ? view + recv_view[p] : g->recv.bytes() + recv_off[p];
-        st = nccl_check(g, ncclRecv(dst, recv_counts[p], ncclUint8, p, g->comm, g->s_comm), deadline, "ncclRecv");
+      if (k * W < recv_counts[p]) {
+        const uint64_t n = std::min(W, recv_counts[p] - k * W);
+        uint8_t* dst = direct[p] ? view + recv_view[p] + k * W : g->recv.bytes() + (buf * peers.size() + si) * recv_slot;
+        st = nccl_check(g, ncclRecv(dst, n, ncclUint8, p, g->comm, g->s_comm), deadline, "ncclRecv");
         if (st != TCX_OK) return st;
-        received += recv_counts[p];
+        received += n;
       }
     }
     if ((st = nccl_check(g, ncclGroupEnd(), deadline, "exchange")) != TCX_OK) return st;
-    if (xp.n_scatter &&
-        (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter, xp.n_scatter, dprefix, g->s_comm)) != TCX_OK)
+    TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
+    const uint64_t ns = scat_off[k + 1] - scat_off[k];
+    if (ns && (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter + scat_off[k], ns,
+                                     prefix_for(o_scatter + scat_off[k]), g->s_comm)) != TCX_OK)
       return st;
   }
   for (uint64_t i = 0; i < plan->n_permutes; ++i) {
@@ -476,8 +564,8 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     st = nccl_check(g, ncclAllGather(g->digests_mine.p, g->digests_all.p, max_n * 32, ncclUint8, g->comm, g->s_comm),
                     deadline, "digest all-gather");
     if (st != TCX_OK) return st;
-    if ((st = launch_copy_jobs(g->digests_all.p, g->digests_compact.p, dj + o_compact, compact.size(), dprefix,
-                               g->s_comm)) != TCX_OK)
+    if ((st = launch_copy_jobs(g->digests_all.p, g->digests_compact.p, dj + o_compact, compact.size(),
+                               prefix_for(o_compact), g->s_comm)) != TCX_OK)
       return st;
     leaf_digests = g->digests_compact.bytes();
   }

@@ -39,7 +39,7 @@ def _jobs_concat(rank_jobs: list) -> tuple[np.ndarray, np.ndarray]:
 class _Plan:
     """A tcx_load_plan with its arrays kept alive."""
 
-    def __init__(self, total, leaf, bounds, rank_jobs, permutes=(), view_bytes=0, slab_bytes=0):
+    def __init__(self, total, leaf, bounds, rank_jobs, permutes=(), view_bytes=0, slab_bytes=0, window_bytes=0):
         self.bounds = np.ascontiguousarray(bounds, dtype=np.uint64)
         self.jobs, self.job_offsets = _jobs_concat(rank_jobs)
         self.perms = permute_array(list(permutes)) if permutes else None
@@ -48,7 +48,7 @@ class _Plan:
             jobs=self.jobs.ctypes.data, job_offsets=self.job_offsets.ctypes.data,
             permutes=self.perms.ctypes.data if self.perms is not None else None,
             n_permutes=0 if self.perms is None else len(self.perms), view_bytes=int(view_bytes),
-            slab_bytes=int(slab_bytes))
+            slab_bytes=int(slab_bytes), window_bytes=int(window_bytes))
 
 
 def plan_exchange(total, leaf, bounds, rank_jobs, rank, view_bytes=0) -> dict:
@@ -153,11 +153,11 @@ class Group:
         return cls(world, rank, device, obj[0] if world > 1 else None, timeout_ms)
 
     def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, permutes=(), view_bytes=None,
-             expected_root: bytes | None = None, slab_bytes: int = 0) -> dict:
+             expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0) -> dict:
         """Runs one load; returns the result fields as a dict. h_stage None: device-resident."""
         if view_bytes is None:
             view_bytes = d_view.numel() * d_view.element_size() if isinstance(d_view, torch.Tensor) else 0
-        plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes)
+        plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes, window_bytes)
         res = _native.LoadResult()
         exp = None
         if expected_root is not None:

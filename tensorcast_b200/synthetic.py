@@ -97,3 +97,70 @@ def write_safetensors(path: str, shapes: dict, seed: int, device=None, chunk_byt
                 pending, pending_bytes = [], 0
     os.replace(tmp, path)
     return {"path": path, "payload_offset": 8 + len(raw), "total_bytes": off, "device": str(device)}
+
+
+def safetensors_layout(shapes: dict) -> tuple[bytes, dict]:
+    """(header bytes incl. the 8-byte length, name -> (payload offset, nbytes)), sorted-name order."""
+    names = sorted(shapes, key=lambda s: s.encode("utf-8"))
+    header, off, where = {}, 0, {}
+    for n in names:
+        nb = 2 * _numel(shapes[n])
+        header[n] = {"dtype": "BF16", "shape": list(shapes[n]), "data_offsets": [off, off + nb]}
+        where[n] = (off, nb)
+        off += nb
+    raw = json.dumps(header, separators=(",", ":")).encode()
+    raw += b" " * ((8 - (8 + len(raw)) % 8) % 8)
+    return struct.pack("<Q", len(raw)) + raw, where
+
+
+def write_safetensors_parallel(path: str, shapes: dict, seed: int, world: int, rank: int, device=None,
+                               timeout_s: float = 1800.0) -> dict:
+    """The same bytes as write_safetensors, written by `world` cooperating processes: rank 0
+    writes the header and sizes the file, then every rank generates the tensors k with
+    k % world == rank (k in sorted-name order) and writes them in place. Progress is
+    coordinated with marker files next to `path`; returns once every rank has finished."""
+    import time
+    if device is None:
+        device = "cuda" if torch.cuda.is_available() else "cpu"
+    head, where = safetensors_layout(shapes)
+    total = sum(nb for _, nb in where.values())
+    tmp = path + ".partial"
+    ready = tmp + ".ready"
+    if rank == 0:
+        for stale in [ready] + [f"{tmp}.done{r}" for r in range(world)]:
+            if os.path.exists(stale):
+                os.unlink(stale)
+        with open(tmp, "wb") as f:
+            f.write(head)
+            f.truncate(len(head) + total)
+        open(ready, "w").close()
+    t0 = time.time()
+    while not os.path.exists(ready):
+        if time.time() - t0 > timeout_s:
+            raise TimeoutError("rank 0 did not create the artifact file")
+        time.sleep(0.2)
+    names = sorted(shapes, key=lambda s: s.encode("utf-8"))
+    fd = os.open(tmp, os.O_WRONLY)
+    try:
+        for k, n in enumerate(names):
+            if k % world != rank:
+                continue
+            t = tensor_data(n, shapes[n], k, seed, device)
+            buf = t.reshape(-1).view(torch.uint8).cpu().numpy()
+            off = len(head) + where[n][0]
+            mv = memoryview(buf)
+            done = 0
+            while done < len(mv):
+                done += os.pwrite(fd, mv[done:], off + done)
+    finally:
+        os.close(fd)
+    open(f"{tmp}.done{rank}", "w").close()
+    if rank == 0:
+        while not all(os.path.exists(f"{tmp}.done{r}") for r in range(world)):
+            if time.time() - t0 > timeout_s:
+                raise TimeoutError("a rank did not finish writing the artifact")
+            time.sleep(0.2)
+        os.replace(tmp, path)
+        for m in [ready] + [f"{tmp}.done{r}" for r in range(world)]:
+            os.unlink(m)
+    return {"path": path, "payload_offset": len(head), "total_bytes": total, "device": str(device)}

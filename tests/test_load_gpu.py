@@ -145,7 +145,8 @@ def test_load_from_registered_file_mapping(cuda_device, tmp_path):
     canon, meta = oviews.canonical_bytes(random_tensors(9, n=30))
     index = index_from_meta(meta, canon.size)
     plan = plan_view(index)
-    path = tmp_path / "blob.bin"
+    base = "/dev/shm" if os.path.isdir("/dev/shm") else str(tmp_path)
+    path = os.path.join(base, f"tcx_map_test_{os.getpid()}.bin")
     head = 4096 + 123  # the staged range starts at an unaligned file offset
     with open(path, "wb") as f:
         f.write(b"\0" * head)
@@ -153,6 +154,7 @@ def test_load_from_registered_file_mapping(cuda_device, tmp_path):
     try:
         m = FileMapping(str(path), head, canon.size, register=True)
     except _native.TcxError as e:
+        os.unlink(path)
         pytest.skip(f"driver does not register file mappings here: {e}")
     g = Group(1, 0, 0)
     try:
@@ -165,3 +167,4 @@ def test_load_from_registered_file_mapping(cuda_device, tmp_path):
     finally:
         g.close()
         m.close()
+        os.unlink(path)
