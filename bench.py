@@ -101,27 +101,45 @@ def artifact_path(args) -> str:
     return os.path.join(args.dir, f"{args.model}-seed{SEED}.safetensors")
 
 
-def ensure_artifact(args, rank: int, local_rank: int) -> str:
-    """Rank 0 writes the artifact once (marker file); the other ranks wait for it."""
-    from tensorcast_b200.synthetic import LLAMA3_70B, LLAMA3_8B, artifact_bytes, llama_shapes, write_safetensors
-    cfg = LLAMA3_8B if args.model == "llama3-8b" else LLAMA3_70B
-    shapes = llama_shapes(cfg)
+TRANSPOSED_O_PROJ = "model.layers.0.self_attn.o_proj.weight"
+
+
+def model_shapes(model: str) -> dict:
+    """BASELINE shapes: Llama-3-8B (config 2/3) or Llama-3-70B (config 4, whose layer-0 o_proj is
+    stored as [in, out] and read through a transpose view)."""
+    from tensorcast_b200.synthetic import LLAMA3_70B, LLAMA3_8B, llama_shapes
+    if model == "llama3-8b":
+        return llama_shapes(LLAMA3_8B)
+    return llama_shapes(LLAMA3_70B, transposed=(TRANSPOSED_O_PROJ,))
+
+
+def ensure_artifact(args, rank: int, local_rank: int, world: int = 1) -> str:
+    """Writes the artifact once (marker file): rank 0 alone, or every rank its share of the
+    tensors when several ranks start together; the other ranks wait for the marker."""
+    from tensorcast_b200.synthetic import artifact_bytes, write_safetensors, write_safetensors_parallel
+    shapes = model_shapes(args.model)
     path = artifact_path(args)
     marker = path + ".done"
-    if rank == 0 and not os.path.exists(marker):
+    if not os.path.exists(marker) and (rank == 0 or world > 1):
         import torch
         os.makedirs(args.dir, exist_ok=True)
-        need = artifact_bytes(shapes) + (64 << 20)
-        st = os.statvfs(args.dir)
-        if st.f_bavail * st.f_frsize < need:
-            raise SystemExit(f"not enough space in {args.dir} for the {need / 1e9:.1f} GB artifact "
-                             f"(set TCX_BENCH_DIR)")
+        if rank == 0:
+            need = artifact_bytes(shapes) + (64 << 20)
+            st = os.statvfs(args.dir)
+            if st.f_bavail * st.f_frsize < need:
+                raise SystemExit(f"not enough space in {args.dir} for the {need / 1e9:.1f} GB artifact "
+                                 f"(set TCX_BENCH_DIR)")
         t0 = time.time()
         dev = f"cuda:{local_rank}" if torch.cuda.is_available() else "cpu"
-        info = write_safetensors(path, shapes, SEED, device=dev)
-        with open(marker, "w") as f:
-            json.dump(info, f)
-        log(f"wrote {info['total_bytes'] / 1e9:.2f} GB artifact in {time.time() - t0:.1f}s ({dev})")
+        if world > 1:
+            info = write_safetensors_parallel(path, shapes, SEED, world, rank, device=dev)
+        else:
+            info = write_safetensors(path, shapes, SEED, device=dev)
+        if rank == 0:
+            with open(marker, "w") as f:
+                json.dump(info, f)
+            log(f"wrote {info['total_bytes'] / 1e9:.2f} GB artifact in {time.time() - t0:.1f}s ({dev}, "
+                f"{world} writer(s))")
     t0 = time.time()
     while not os.path.exists(marker):
         if time.time() - t0 > 900:
@@ -293,7 +311,7 @@ def main() -> None:
     except Exception as e:  # noqa: BLE001
         n_local_cpus = 0
         log(f"CPU binding unavailable: {e}")
-    path = ensure_artifact(args, rank, local)
+    path = ensure_artifact(args, rank, local, world)
     if world > 1:
         import datetime
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
@@ -314,8 +332,14 @@ def main() -> None:
     canonical_is_payload = len(whole) == 1 and whole[0][3] == T
     # Every rank's view: identity at N=1, the tensor-parallel shards otherwise.
     plans = []
+    transposed = TRANSPOSED_O_PROJ if args.model == "llama3-70b" else None
     for r in range(world):
-        spec = None if world == 1 else build_view_spec(index, slices=tp_slices(index, world, r))
+        slices = {} if world == 1 else tp_slices(index, world, r)
+        tr = None
+        if transposed:
+            slices.pop(transposed, None)
+            tr = {transposed: [(0, 1)]}
+        spec = None if not slices and not tr else build_view_spec(index, slices=slices, transpose=tr)
         plans.append(plan_view(index, spec))
     mine = plans[rank]
     rank_jobs = [p.jobs for p in plans]
@@ -384,7 +408,7 @@ def main() -> None:
             if cpu_root != root:
                 raise SystemExit(f"PARITY FAILURE: GPU root {root.hex()} != CPU oracle {cpu_root.hex()}")
     # Views: check a fixed sample of tensors against numpy slicing of the file.
-    view_ok = verify_view_sample(path, index, mine, d_view, world, rank, whole)
+    view_ok = verify_view_sample(path, index, mine, d_view, world, rank, whole, transposed)
     if world > 1:
         ok = torch.tensor([1 if view_ok else 0], device="cuda")
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
@@ -566,7 +590,7 @@ def run_kv(args) -> None:
         dist.destroy_process_group()
 
 
-def verify_view_sample(path, index, plan, d_view, world, rank, whole) -> bool:
+def verify_view_sample(path, index, plan, d_view, world, rank, whole, transposed=None) -> bool:
     """Compares a deterministic sample of view tensors with numpy slicing of the file."""
     import numpy as np
     import torch
@@ -579,7 +603,9 @@ def verify_view_sample(path, index, plan, d_view, world, rank, whole) -> bool:
             continue
         st = src[t.name]
         arr = np.memmap(path, dtype=np.uint16, mode="r", offset=st.file_offset, shape=st.shape)
-        if world > 1:
+        if t.name == transposed:
+            arr = arr.T
+        elif world > 1:
             e = index.entries[t.name]
             if any(k in t.name for k in ("o_proj", "down_proj")):
                 ln = e.shape[1] // world

@@ -353,11 +353,13 @@ typedef struct tcx_load_result {
 /* Runs one collective load on every rank of g (all ranks call it with the same
  * plan). h_stage: this rank's staged bytes in pinned host memory, or NULL when
  * d_stage already holds them (device-resident load: no H2D). d_view may equal
- * d_stage when every job of this rank is an in-place identity. Synchronous.
+ * d_stage when every job of this rank is an in-place identity. The load starts
+ * after the work already queued on `stream` (the caller's stream, NULL = the
+ * legacy default stream) and the call returns once it is complete.
  * expected_root (32 bytes, may be NULL): a mismatch returns DATA_LOSS
  * (verification_stage.cc:130-141). */
 tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage, void* d_view,
-                          const uint8_t* expected_root, tcx_load_result* out);
+                          const uint8_t* expected_root, tcx_load_result* out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Paged KV-cache gather (no reference counterpart: the reference stores

@@ -133,7 +133,7 @@ _SIGNATURES = {
     "tcx_group_create": (_c.c_int, [_c.c_void_p, _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.POINTER(_c.c_void_p)]),
     "tcx_group_destroy": (_c.c_int, [_c.c_void_p]),
     "tcx_group_load": (_c.c_int, [_c.c_void_p, _c.POINTER(LoadPlan), _c.c_void_p, _c.c_void_p, _c.c_void_p,
-                                  _c.c_void_p, _c.POINTER(LoadResult)]),
+                                  _c.c_void_p, _c.POINTER(LoadResult), _c.c_void_p]),
 }
 
 

@@ -297,7 +297,8 @@ extern "C" tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n
 }
 
 extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage,
-                                     void* d_view, const uint8_t* expected_root, tcx_load_result* out) {
+                                     void* d_view, const uint8_t* expected_root, tcx_load_result* out,
+                                     void* stream) {
   if (g == nullptr) return set_error(TCX_INVALID_ARGUMENT, "group is null");
   if (g->world > 1 && g->comm == nullptr)
     return set_error(TCX_FAILED_PRECONDITION, "group communicator was aborted by an earlier failure");
@@ -458,7 +459,10 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   const auto deadline = Clock::now() + std::chrono::milliseconds(g->timeout_ms);
 
   // --- H2D + hashing ---------------------------------------------------------
-  TCX_CUDA_TRY(cudaEventRecord(g->ev_start, g->s_copy));
+  // Everything queued on the caller's stream before this call (writes into the
+  // staged or view buffers, for instance) completes before the load touches them.
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_start, static_cast<cudaStream_t>(stream)));
+  TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_copy, g->ev_start, 0));
   TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_hash, g->ev_start, 0));
   TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->ev_start, 0));
   uint64_t h2d_bytes = 0;

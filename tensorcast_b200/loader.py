@@ -165,8 +165,9 @@ class Group:
                 raise ValueError("expected_root must be 32 bytes")
             exp = ctypes.create_string_buffer(bytes(expected_root), 32)
         ptr = lambda x: None if x is None else (x.data_ptr() if hasattr(x, "data_ptr") else int(x))  # noqa: E731
+        stream = torch.cuda.current_stream().cuda_stream
         _native.call("tcx_group_load", self._h, ctypes.byref(plan.c), ptr(h_stage), ptr(d_stage), ptr(d_view), exp,
-                     ctypes.byref(res))
+                     ctypes.byref(res), stream)
         return {"root": bytes(res.root), "multihash": res.multihash.decode(), "leaves": res.leaves,
                 "h2d_bytes": res.h2d_bytes, "peer_send_bytes": res.peer_send_bytes,
                 "peer_recv_bytes": res.peer_recv_bytes, "h2d_ms": res.h2d_ms, "hash_ms": res.hash_ms,
