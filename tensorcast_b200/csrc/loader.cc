@@ -449,9 +449,14 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   std::copy(compact.begin(), compact.end(), hj + o_compact);
   auto* dj = static_cast<tcx_copy_job*>(g->jobs.p);
   auto* dprefix = static_cast<uint64_t*>(g->prefix.p);
-  uint64_t launch_idx = 0;
-  // Each copy-job launch gets its own prefix region (launches run on two streams).
-  auto prefix_for = [&](uint64_t job_off) { return dprefix + job_off + (launch_idx++); };
+  // Each copy-job launch gets its own prefix region, handed out in launch order
+  // (launches run on two streams at once, so regions must never overlap).
+  uint64_t prefix_cursor = 0;
+  auto prefix_for = [&](uint64_t n_jobs) {
+    uint64_t* r = dprefix + prefix_cursor;
+    prefix_cursor += n_jobs + 1;
+    return r;
+  };
   auto* view = static_cast<uint8_t*>(d_view);
   auto* stage = static_cast<uint8_t*>(d_stage);
   const auto* hstage = static_cast<const uint8_t*>(h_stage);
@@ -510,7 +515,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   for (uint64_t k = 0; k < xp.n_gaps; ++k)
     TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
   if (!local_kept.empty() &&
-      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(o_local), g->s_comm)) != TCX_OK)
+      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), g->s_comm)) != TCX_OK)
     return st;
   uint64_t sent = 0, received = 0;
   for (uint64_t k = 0; k < rounds; ++k) {
@@ -519,7 +524,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     if (k >= 2) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->sent_events[k - 2], 0));
     const uint64_t np = pack_off[k + 1] - pack_off[k];
     if (np && (st = launch_copy_jobs(stage, g->send.p, dj + o_pack + pack_off[k], np,
-                                     prefix_for(o_pack + pack_off[k]), g->s_pack)) != TCX_OK)
+                                     prefix_for(np), g->s_pack)) != TCX_OK)
       return st;
     TCX_CUDA_TRY(cudaEventRecord(g->packed_events[k], g->s_pack));
     TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[k], 0));
@@ -546,7 +551,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
     const uint64_t ns = scat_off[k + 1] - scat_off[k];
     if (ns && (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter + scat_off[k], ns,
-                                     prefix_for(o_scatter + scat_off[k]), g->s_comm)) != TCX_OK)
+                                     prefix_for(ns), g->s_comm)) != TCX_OK)
       return st;
   }
   for (uint64_t i = 0; i < plan->n_permutes; ++i) {
@@ -569,7 +574,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
                     deadline, "digest all-gather");
     if (st != TCX_OK) return st;
     if ((st = launch_copy_jobs(g->digests_all.p, g->digests_compact.p, dj + o_compact, compact.size(),
-                               prefix_for(o_compact), g->s_comm)) != TCX_OK)
+                               prefix_for(compact.size()), g->s_comm)) != TCX_OK)
       return st;
     leaf_digests = g->digests_compact.bytes();
   }

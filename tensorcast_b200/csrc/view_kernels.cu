@@ -78,10 +78,13 @@ __global__ void __launch_bounds__(kCopyThreads) copy_jobs_kernel(const uint8_t* 
   for (uint64_t w = blockIdx.x; w < total; w += gridDim.x) {
     if (threadIdx.x == 0) s_job = find_job(prefix, n, w);
     __syncthreads();
-    const tcx_copy_job j = jobs[s_job];
+    const uint64_t ji = s_job;
     __syncthreads();
+    if (ji >= n) continue;  // inconsistent prefix: never index past the job table
+    const tcx_copy_job j = jobs[ji];
     const uint64_t bytes = j.rows * j.row_bytes;
-    const uint64_t c0 = (w - prefix[s_job]) * kCopyChunk;
+    const uint64_t c0 = (w - prefix[ji]) * kCopyChunk;
+    if (w < prefix[ji] || c0 >= bytes) continue;  // never copy outside the job
     const uint64_t c1 = min(c0 + kCopyChunk, bytes);
     const bool vec = ((j.src_off | j.dst_off | j.src_pitch | j.dst_pitch | j.row_bytes) & 15u) == 0 &&
                      ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0;
