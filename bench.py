@@ -462,7 +462,9 @@ def main() -> None:
                 "workload": (f"{args.model}-shaped bf16 safetensors (seed {SEED}), {T} B, identity view"
                              if world == 1 else
                              f"{args.model}-shaped bf16 safetensors (seed {SEED}), {T} B, TP-{world} views "
-                             f"(q/k/v/gate/up/embed/lm_head dim 0, o/down dim 1)"),
+                             f"(q/k/v/gate/up/embed/lm_head dim 0, o/down dim 1)"
+                             + (f"; {transposed} stored [in, out] and read whole through a transpose view"
+                                if transposed else "")),
                 "artifact_bytes": T, "leaf_bytes": L, "leaves": first["leaves"],
                 "view_bytes_per_rank": mine.view_bytes, "parallelism": f"tp{world}",
                 "l2": "inputs (staged bytes) far larger than the 126 MB L2; no flush needed",
