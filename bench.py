@@ -57,6 +57,9 @@ def parse_args():
     ap.add_argument("--workload", choices=["artifact", "kv"], default="artifact",
                     help="artifact: the collective from-disk load (default); kv: BASELINE config 5, paged KV "
                          "gather + per-sequence hash, 8 sequence shards dealt to the ranks")
+    ap.add_argument("--copy-only", metavar="ROWS:COLS:TP",
+                    help="only time the view kernels on a bf16 [ROWS, COLS] tensor: the dim-0 and dim-1 "
+                         "tensor-parallel shards of rank 0 of TP (copy jobs) and a full transpose")
     ap.add_argument("--hash-only", metavar="BYTES:LEAF",
                     help="only time the SHA-256 leaf kernel on BYTES of seeded device data (e.g. 512M:128K); "
                          "the small case used for ncu captures")
@@ -88,6 +91,52 @@ def run_hash_only(args) -> None:
     ms = e0.elapsed_time(e1) / args.steps
     print(json.dumps({"mode": "hash-only", "bytes": nbytes, "leaf": leaf, "leaves": n, "ms": round(ms, 3),
                       "gbs": round(nbytes / ms / 1e6, 2)}), flush=True)
+
+
+def run_copy_only(args) -> None:
+    """HBM-bound view kernels alone: algorithmic bytes = bytes read + bytes written."""
+    import ctypes
+    import numpy as np
+    import torch
+    from tensorcast_b200 import _native
+    from tensorcast_b200.views import JOB_DTYPE
+    rows, cols, tp = (int(v) for v in args.copy_only.split(":"))
+    es = 2
+    g = torch.Generator(device="cuda").manual_seed(0)
+    src = torch.randint(0, 256, (rows * cols * es,), dtype=torch.uint8, device="cuda", generator=g)
+    L = _native.lib()
+    s = torch.cuda.current_stream()
+    res = {"mode": "copy-only", "rows": rows, "cols": cols, "tp": tp}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 1)):
+            fn()
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(args.steps):
+            fn()
+        e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    for name, job in (("dim0_shard", (0, 0, cols * es * rows // tp, cols * es * rows // tp, cols * es * rows // tp, 1)),
+                      ("dim1_shard", (0, 0, cols * es, cols * es // tp, cols * es // tp, rows))):
+        jobs = torch.from_numpy(np.array([job], dtype=JOB_DTYPE).view(np.uint8)).cuda()
+        nbytes = job[4] * job[5]
+        dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        sb = int(L.tcx_copy_jobs_scratch_bytes(1))
+        scratch = torch.empty(sb, dtype=torch.uint8, device="cuda")
+        ms = timed(lambda: _native.call("tcx_copy_jobs", src.data_ptr(), dst.data_ptr(), jobs.data_ptr(), 1,
+                                        scratch.data_ptr(), sb, s.cuda_stream))
+        res[name] = {"bytes_moved": 2 * nbytes, "ms": round(ms, 4), "gbs": round(2 * nbytes / ms / 1e6, 1)}
+    out = torch.empty_like(src)
+    pj = _native.PermuteJob(0, 0, es, 2)
+    pj.shape[0], pj.shape[1], pj.perm[0], pj.perm[1] = rows, cols, 1, 0
+    ms = timed(lambda: _native.call("tcx_permute", src.data_ptr(), out.data_ptr(), ctypes.byref(pj), s.cuda_stream))
+    res["transpose"] = {"bytes_moved": 2 * src.numel(), "ms": round(ms, 4), "gbs": round(2 * src.numel() / ms / 1e6, 1)}
+    res["hbm_gbs"] = measured_hbm()
+    print(json.dumps(res), flush=True)
 
 
 def log(*a):
@@ -288,6 +337,9 @@ def main() -> None:
     args = parse_args()
     if args.hash_only:
         run_hash_only(args)
+        return
+    if args.copy_only:
+        run_copy_only(args)
         return
     if args.workload == "kv":
         run_kv(args)

@@ -268,7 +268,14 @@ typedef struct tcx_load_plan {
   uint64_t slab_bytes;           /* bytes per leaf per H2D/hash slab (0: 256 KiB) */
   uint64_t window_bytes;         /* bytes per peer per exchange round; bounds the send/receive
                                     scratch to about 2*(N-1) windows (0: 512 MiB) */
+  uint64_t flags;                /* TCX_LOAD_* bits */
 } tcx_load_plan;
+
+/* tcx_load_plan.flags: also compute the data multihash of this rank's finished
+ * view (leaf size from tcx_leaf_policy(view_bytes, 4 MiB)), as the reference's
+ * ViewHashComputer::hash_replica_view does for a GPU-resident view
+ * (core/store/materialization/common/view_hash_utils.cc:38-82). */
+#define TCX_LOAD_VIEW_HASH 1ull
 
 /* Per-peer sizes and job lists of the exchange for one rank (host-only planning).
  * Capacities: tcx_plan_exchange_capacity(). pack_jobs move this rank's staged
@@ -348,6 +355,8 @@ typedef struct tcx_load_result {
   uint64_t h2d_bytes;   /* host-to-device bytes of this rank */
   uint64_t peer_send_bytes, peer_recv_bytes;
   float h2d_ms, hash_ms, exchange_ms, total_ms;  /* device-timed phases on this rank */
+  char view_multihash[64];  /* with TCX_LOAD_VIEW_HASH: data multihash of this rank's view, else "" */
+  uint64_t view_leaf_bytes; /* leaf size used for view_multihash */
 } tcx_load_result;
 
 /* Runs one collective load on every rank of g (all ranks call it with the same

@@ -74,7 +74,7 @@ class LoadPlan(ctypes.Structure):
     _fields_ = [("total_bytes", _c.c_uint64), ("leaf_bytes", _c.c_uint64), ("stage_bounds", _c.c_void_p),
                 ("jobs", _c.c_void_p), ("job_offsets", _c.c_void_p), ("permutes", _c.c_void_p),
                 ("n_permutes", _c.c_uint64), ("view_bytes", _c.c_uint64), ("slab_bytes", _c.c_uint64),
-                ("window_bytes", _c.c_uint64)]
+                ("window_bytes", _c.c_uint64), ("flags", _c.c_uint64)]
 
 
 class ExchangePlan(ctypes.Structure):
@@ -89,7 +89,7 @@ class LoadResult(ctypes.Structure):
     _fields_ = [("root", _c.c_uint8 * 32), ("multihash", _c.c_char * 64), ("leaves", _c.c_uint64),
                 ("h2d_bytes", _c.c_uint64), ("peer_send_bytes", _c.c_uint64), ("peer_recv_bytes", _c.c_uint64),
                 ("h2d_ms", _c.c_float), ("hash_ms", _c.c_float), ("exchange_ms", _c.c_float),
-                ("total_ms", _c.c_float)]
+                ("total_ms", _c.c_float), ("view_multihash", _c.c_char * 64), ("view_leaf_bytes", _c.c_uint64)]
 
 
 # Every function exported by include/tcx.h with (restype, argtypes).

@@ -80,7 +80,7 @@ struct tcx_group {
   ncclComm_t comm = nullptr;
   cudaStream_t s_copy = nullptr, s_hash = nullptr, s_comm = nullptr, s_pack = nullptr;
   DevBuf digests_mine, states, digests_all, digests_compact, merkle_scratch, root, send, recv, perm_scratch, jobs,
-      prefix;
+      prefix, view_digests, view_scratch;
   uint8_t* h_root = nullptr;
   tcx_copy_job* h_jobs = nullptr;
   uint64_t h_jobs_cap = 0;
@@ -225,7 +225,7 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
     g->comm = nullptr;
   }
   for (DevBuf* b : {&g->digests_mine, &g->states, &g->digests_all, &g->digests_compact, &g->merkle_scratch, &g->root,
-                    &g->send, &g->recv, &g->perm_scratch, &g->jobs, &g->prefix})
+                    &g->send, &g->recv, &g->perm_scratch, &g->jobs, &g->prefix, &g->view_digests, &g->view_scratch})
     b->release();
   if (g->h_root) cudaFreeHost(g->h_root);
   if (g->h_jobs) cudaFreeHost(g->h_jobs);
@@ -431,6 +431,14 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     if ((st = g->digests_all.grow(static_cast<uint64_t>(world) * max_n * 32)) != TCX_OK) return st;
     if ((st = g->digests_compact.grow(n_total * 32)) != TCX_OK) return st;
   }
+  const bool view_hash = (plan->flags & TCX_LOAD_VIEW_HASH) != 0 && plan->view_bytes > 0;
+  uint64_t view_leaf = 0, view_n = 0;
+  if (view_hash) {
+    if ((st = tcx_leaf_policy(plan->view_bytes, TCX_DEFAULT_LEAF_BYTES, &view_leaf)) != TCX_OK) return st;
+    view_n = (plan->view_bytes + view_leaf - 1) / view_leaf;
+    if ((st = g->view_digests.grow(view_n * 32)) != TCX_OK) return st;
+    if ((st = g->view_scratch.grow(merkle_scratch_bytes(view_n) + 256)) != TCX_OK) return st;
+  }
   if ((st = ensure_events(g->packed_events, rounds)) != TCX_OK) return st;
   if ((st = ensure_events(g->sent_events, rounds)) != TCX_OK) return st;
   if (n_jobs_all > g->h_jobs_cap) {
@@ -564,6 +572,15 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     if ((st = launch_permute(view, g->perm_scratch.p, pj, g->s_comm)) != TCX_OK) return st;
     TCX_CUDA_TRY(cudaMemcpyAsync(view + off, g->perm_scratch.p, bytes, cudaMemcpyDeviceToDevice, g->s_comm));
   }
+  if (view_hash) {
+    // View multihash: the view is final here; its root lands after the artifact root.
+    if ((st = launch_leaf_pass(view, plan->view_bytes, view_leaf, static_cast<uint32_t>(view_n), 0, ~0ull, nullptr,
+                               g->view_digests.p, g->s_comm)) != TCX_OK)
+      return st;
+    if ((st = launch_merkle(g->view_digests.bytes(), view_n, g->view_scratch.bytes(), g->root.bytes() + 64,
+                            g->s_comm)) != TCX_OK)
+      return st;
+  }
   TCX_CUDA_TRY(cudaEventRecord(g->ev_exch, g->s_comm));
 
   // --- digests of every rank, Merkle root ------------------------------------
@@ -580,7 +597,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   }
   if ((st = launch_merkle(leaf_digests, n_total, g->merkle_scratch.bytes(), g->root.bytes(), g->s_comm)) != TCX_OK)
     return st;
-  TCX_CUDA_TRY(cudaMemcpyAsync(g->h_root, g->root.p, 32, cudaMemcpyDeviceToHost, g->s_comm));
+  TCX_CUDA_TRY(cudaMemcpyAsync(g->h_root, g->root.p, view_hash ? 96 : 32, cudaMemcpyDeviceToHost, g->s_comm));
   TCX_CUDA_TRY(cudaEventRecord(g->ev_end, g->s_comm));
   if ((st = wait_event(g, g->ev_end, deadline)) != TCX_OK) return st;
 
@@ -595,6 +612,10 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   out->hash_ms = elapsed_ms(g->ev_start, g->ev_hash);
   out->exchange_ms = elapsed_ms(g->ev_h2d, g->ev_exch);
   out->total_ms = elapsed_ms(g->ev_start, g->ev_end);
+  if (view_hash) {
+    encode_multihash(g->h_root + 64, out->view_multihash);
+    out->view_leaf_bytes = view_leaf;
+  }
   if (expected_root != nullptr && std::memcmp(expected_root, out->root, 32) != 0)
     return set_error(TCX_DATA_LOSS, "ARTIFACT_ID_MISMATCH: data multihash of the loaded bytes differs from the expected one");
   return TCX_OK;

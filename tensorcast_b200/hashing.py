@@ -107,3 +107,31 @@ def prewarm_gpu_hash_for_device(device_id: int) -> None:
 
 def prewarm_gpu_hash_for_visible_devices() -> None:
     _native.call("tcx_prewarm_visible_devices")
+
+
+def compute_canonical_leaf_digests(src: torch.Tensor, leaf_indices, chunk_bytes: int, *, nbytes: int | None = None,
+                                   stream=None) -> list[bytes]:
+    """Digests of the given leaves of a device buffer, in the order asked for.
+
+    Mirrors compute_canonical_leaf_digests for GPU memory
+    (core/store/materialization/dataplane/verification/verification_utils.cc:337-369, 851-868):
+    leaf i is [i*chunk_bytes, (i+1)*chunk_bytes); indices whose leaf would run past the
+    buffer are skipped (no entry). The reference copies each leaf to the host and hashes
+    it there; here all leaves are hashed in one tcx_sha256_leaf_table launch and only the
+    32-byte digests come back."""
+    import numpy as np
+    if chunk_bytes <= 0:
+        raise ValueError("chunk_bytes must be > 0")
+    total = src.numel() * src.element_size() if nbytes is None else int(nbytes)
+    idx = [int(i) for i in leaf_indices if (int(i) + 1) * chunk_bytes <= total]
+    if not idx:
+        return []
+    if chunk_bytes > 0xFFFFFFFF:
+        raise ValueError("chunk_bytes must fit in 32 bits")
+    offs = torch.from_numpy(np.asarray(idx, dtype=np.uint64).view(np.int64) * chunk_bytes).to(src.device)
+    lens = torch.full((len(idx),), chunk_bytes, dtype=torch.int64).to(torch.int32).to(src.device)
+    out = torch.empty((len(idx), 32), dtype=torch.uint8, device=src.device)
+    aligned = src.data_ptr() % 16 == 0 and chunk_bytes % 16 == 0
+    _native.call("tcx_sha256_leaf_table", src.data_ptr(), offs.data_ptr(), lens.data_ptr(), len(idx), int(aligned),
+                 out.data_ptr(), _stream_handle(stream))
+    return [bytes(r) for r in out.cpu().numpy()]

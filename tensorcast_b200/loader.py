@@ -18,6 +18,9 @@ from . import _native
 from .views import JOB_DTYPE, permute_array
 
 
+VIEW_HASH = 1  # TCX_LOAD_VIEW_HASH
+
+
 def stage_bounds(total: int, leaf: int, world: int) -> list[int]:
     """Leaf-aligned split of [0, total) into `world` contiguous ranges (rank r stages
     leaves [r*n//world, (r+1)*n//world))."""
@@ -39,7 +42,8 @@ def _jobs_concat(rank_jobs: list) -> tuple[np.ndarray, np.ndarray]:
 class _Plan:
     """A tcx_load_plan with its arrays kept alive."""
 
-    def __init__(self, total, leaf, bounds, rank_jobs, permutes=(), view_bytes=0, slab_bytes=0, window_bytes=0):
+    def __init__(self, total, leaf, bounds, rank_jobs, permutes=(), view_bytes=0, slab_bytes=0, window_bytes=0,
+                 flags=0):
         self.bounds = np.ascontiguousarray(bounds, dtype=np.uint64)
         self.jobs, self.job_offsets = _jobs_concat(rank_jobs)
         self.perms = permute_array(list(permutes)) if permutes else None
@@ -48,7 +52,7 @@ class _Plan:
             jobs=self.jobs.ctypes.data, job_offsets=self.job_offsets.ctypes.data,
             permutes=self.perms.ctypes.data if self.perms is not None else None,
             n_permutes=0 if self.perms is None else len(self.perms), view_bytes=int(view_bytes),
-            slab_bytes=int(slab_bytes), window_bytes=int(window_bytes))
+            slab_bytes=int(slab_bytes), window_bytes=int(window_bytes), flags=int(flags))
 
 
 def plan_exchange(total, leaf, bounds, rank_jobs, rank, view_bytes=0) -> dict:
@@ -153,11 +157,13 @@ class Group:
         return cls(world, rank, device, obj[0] if world > 1 else None, timeout_ms)
 
     def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, permutes=(), view_bytes=None,
-             expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0) -> dict:
+             expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0,
+             view_hash: bool = False) -> dict:
         """Runs one load; returns the result fields as a dict. h_stage None: device-resident."""
         if view_bytes is None:
             view_bytes = d_view.numel() * d_view.element_size() if isinstance(d_view, torch.Tensor) else 0
-        plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes, window_bytes)
+        plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes, window_bytes,
+                     flags=VIEW_HASH if view_hash else 0)
         res = _native.LoadResult()
         exp = None
         if expected_root is not None:
@@ -171,7 +177,8 @@ class Group:
         return {"root": bytes(res.root), "multihash": res.multihash.decode(), "leaves": res.leaves,
                 "h2d_bytes": res.h2d_bytes, "peer_send_bytes": res.peer_send_bytes,
                 "peer_recv_bytes": res.peer_recv_bytes, "h2d_ms": res.h2d_ms, "hash_ms": res.hash_ms,
-                "exchange_ms": res.exchange_ms, "total_ms": res.total_ms}
+                "exchange_ms": res.exchange_ms, "total_ms": res.total_ms,
+                "view_multihash": res.view_multihash.decode(), "view_leaf_bytes": res.view_leaf_bytes}
 
     def close(self) -> None:
         if self._h:

@@ -117,3 +117,11 @@ def test_leaf_digests_are_stream_ordered(cuda_device):
         d = tcx.sha256_leaves(dev, 1 << 16, stream=s)
     s.synchronize()
     assert (d.cpu().numpy() == oracle.leaf_digests(a, 1 << 16, openssl=True, threads=8)).all()
+
+
+def test_canonical_leaf_digests_skip_partial_leaves(cuda_device):
+    """verification_utils.cc:337-369: digests of the requested full leaves, in request order."""
+    a = seeded(77, 10 * 4096 + 100)
+    got = tcx.hashing.compute_canonical_leaf_digests(to_dev(a), [3, 0, 9, 10, 11], 4096)
+    want = oracle.leaf_digests(a, 4096)
+    assert got == [want[3].tobytes(), want[0].tobytes(), want[9].tobytes()]  # 10 is partial, 11 beyond

@@ -110,11 +110,13 @@ def test_single_rank_load_random_views(cuda_device, host):
             expected = oracle.tree_root(oracle.leaf_digests(canon, leaf))
             res = g.load(canon.size, leaf, [0, canon.size], [plan.jobs], d_stage=d_stage, d_view=d_view,
                          h_stage=pinned(canon) if host else None, permutes=plan.permutes,
-                         view_bytes=plan.view_bytes, expected_root=expected, slab_bytes=128)
+                         view_bytes=plan.view_bytes, expected_root=expected, slab_bytes=128, view_hash=True)
             assert res["root"] == expected
             assert res["multihash"] == oracle.multihash(expected)
             want = oviews.materialize_view(canon, meta, slices, transpose, subset)
             assert (d_view.cpu().numpy()[: plan.view_bytes] == want).all()
+            # the view hash: the GPU entry's data multihash of the view bytes (adaptive leaf policy)
+            assert res["view_multihash"] == oracle.multihash_gpu_semantics(want)
     finally:
         g.close()
 
