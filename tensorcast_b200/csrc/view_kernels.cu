@@ -94,13 +94,27 @@ __global__ void __launch_bounds__(kCopyThreads) copy_jobs_kernel(const uint8_t* 
       const uint64_t row0 = u0 / upr;
       const uint32_t col0 = static_cast<uint32_t>(u0 - row0 * upr);
       const uint32_t units = static_cast<uint32_t>((c1 - c0) >> 4);
-      for (uint32_t u = threadIdx.x; u < units; u += blockDim.x) {
-        const uint32_t t = col0 + u;
-        const uint32_t dr = t / upr;
-        const uint32_t col = t - dr * upr;
-        const uint64_t row = row0 + dr;
-        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + j.src_off + row * j.src_pitch) + col);
-        __stcs(reinterpret_cast<uint4*>(dst + j.dst_off + row * j.dst_pitch) + col, v);
+      // Four 16-byte loads in flight per thread before their stores.
+      constexpr int kBatch = 4;
+      for (uint32_t base = threadIdx.x; base < units; base += blockDim.x * kBatch) {
+        uint4 v[kBatch];
+        uint64_t doff[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+          const uint32_t u = base + k * blockDim.x;
+          if (u < units) {
+            const uint32_t t = col0 + u;
+            const uint32_t dr = t / upr;
+            const uint32_t col = t - dr * upr;
+            const uint64_t row = row0 + dr;
+            v[k] = __ldcs(reinterpret_cast<const uint4*>(src + j.src_off + row * j.src_pitch) + col);
+            doff[k] = j.dst_off + row * j.dst_pitch + 16ull * col;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+          if (base + k * blockDim.x < units) __stcs(reinterpret_cast<uint4*>(dst + doff[k]), v[k]);
+        }
       }
     } else {
       for (uint64_t b = c0 + threadIdx.x; b < c1; b += blockDim.x) {
