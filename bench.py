@@ -51,6 +51,9 @@ def parse_args():
     ap.add_argument("--leaf", type=int, default=LEAF)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["push", "nccl"], default="push",
+                    help="N>1 shard exchange: push over peer memory (copy kernels writing into the peers' views "
+                         "over NVLink) or NCCL send/recv of packed windows")
     ap.add_argument("--stage", choices=["mapped", "pinned"], default="pinned",
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
                          "(no second host copy), or a pinned copy read with parallel preads")
@@ -434,7 +437,8 @@ def main() -> None:
 
     def load(host: bool, expected=None):
         return group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage if host else None,
-                          permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected)
+                          permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected,
+                          peer_push=args.exchange == "push" and world > 1)
 
     def max_over_ranks(x: float) -> float:
         if world == 1:
@@ -518,6 +522,8 @@ def main() -> None:
                              + (f"; {transposed} stored [in, out] and read whole through a transpose view"
                                 if transposed else "")),
                 "artifact_bytes": T, "leaf_bytes": L, "leaves": first["leaves"],
+                "exchange": ("push over peer memory (NVLink P2P stores from the copy kernels)"
+                             if args.exchange == "push" else "NCCL send/recv of packed windows") if world > 1 else "none",
                 "view_bytes_per_rank": mine.view_bytes, "parallelism": f"tp{world}",
                 "l2": "inputs (staged bytes) far larger than the 126 MB L2; no flush needed",
                 "timing": "device events per step (tcx_group_load), mean over steps, max over ranks"},

@@ -145,8 +145,10 @@ tcx_status tcx_multihash_encode(const uint8_t* digest32, char* out, size_t out_c
  * and compute_data_multihash_from_gpu_memory
  * (core/store/materialization/dataplane/metadata/source_hash.cc:72-78):
  * same argument checks and messages, the tcx_leaf_policy leaf size, and the
- * calling thread's current device is left set to device_id. Synchronous. The
- * digest buffers and the stream are cached per device and reused across calls. */
+ * calling thread's current device is left set to device_id. Synchronous: the
+ * hash starts after the work already queued on the legacy default stream and
+ * the call returns with the result. The digest buffers and the stream are
+ * cached per device and reused across calls. */
 tcx_status tcx_multihash_from_gpu(const void* d_src, uint64_t total_bytes, int device_id, uint64_t leaf_chunk_bytes,
                                   char* out, size_t out_capacity);
 
@@ -276,6 +278,14 @@ typedef struct tcx_load_plan {
  * ViewHashComputer::hash_replica_view does for a GPU-resident view
  * (core/store/materialization/common/view_hash_utils.cc:38-82). */
 #define TCX_LOAD_VIEW_HASH 1ull
+
+/* tcx_load_plan.flags: exchange by pushing over peer memory instead of NCCL
+ * send/recv: every rank maps every peer's view (CUDA IPC; d_view must be memory
+ * this process allocated with cudaMalloc) and its copy kernels write the peers'
+ * view pieces from its staged bytes directly into those views over NVLink, so
+ * extraction and transfer are one pass with no pack or receive buffers. NCCL
+ * carries only the handle exchange and two one-word barriers. */
+#define TCX_LOAD_PEER_PUSH 2ull
 
 /* Per-peer sizes and job lists of the exchange for one rank (host-only planning).
  * Capacities: tcx_plan_exchange_capacity(). pack_jobs move this rank's staged

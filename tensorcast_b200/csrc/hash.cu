@@ -660,6 +660,7 @@ struct DeviceHashContext {
   uint64_t scratch_cap = 0;
   uint8_t* d_root = nullptr;
   uint8_t* h_root = nullptr;  // pinned
+  cudaEvent_t queued = nullptr;  // marks prior work on the legacy default stream
 };
 
 constexpr int kMaxDevices = 64;
@@ -669,6 +670,7 @@ DeviceHashContext g_ctx[kMaxDevices];
 tcx_status ensure_context(DeviceHashContext& ctx, uint64_t n_leaves) {
   if (!ctx.ready) {
     TCX_CUDA_TRY(cudaStreamCreateWithFlags(&ctx.stream, cudaStreamNonBlocking));
+    TCX_CUDA_TRY(cudaEventCreateWithFlags(&ctx.queued, cudaEventDisableTiming));
     TCX_CUDA_TRY(cudaMalloc(&ctx.d_root, 256));
     TCX_CUDA_TRY(cudaMallocHost(&ctx.h_root, 256));
     cudaFuncAttributes attr;
@@ -827,6 +829,14 @@ extern "C" tcx_status tcx_multihash_from_gpu(const void* d_src, uint64_t total_b
   DeviceHashContext& ctx = g_ctx[device_id];
   std::lock_guard<std::mutex> lock(ctx.mu);
   tcx_status st = ensure_context(ctx, n);
+  if (st == TCX_OK) {
+    // The hash runs on the library's own stream; it first waits for the work already
+    // queued on the legacy default stream (which orders every blocking stream), so a
+    // buffer just written there is complete before it is hashed.
+    cudaError_t e = cudaEventRecord(ctx.queued, cudaStreamLegacy);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx.stream, ctx.queued, 0);
+    if (e != cudaSuccess) st = set_error(TCX_INTERNAL, "stream ordering failed: " + cuda_msg(e));
+  }
   if (st == TCX_OK) st = launch_leaves(d_src, total_bytes, leaf, static_cast<uint32_t>(n), ctx.digests, ctx.stream);
   if (st == TCX_OK) st = launch_merkle(ctx.digests, n, ctx.scratch, ctx.d_root, ctx.stream);
   if (st == TCX_OK) {

@@ -15,6 +15,7 @@
 // Reference: collective_disk_loader.cc:5538-5816 runs read -> H2D to one root
 // GPU -> ncclBroadcast/ncclSend per chunk with a host synchronize after every
 // chunk; verification_stage.cc:55-128 hashes the replica afterwards.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <nccl.h>
@@ -86,6 +87,17 @@ struct tcx_group {
   uint64_t h_jobs_cap = 0;
   std::vector<cudaEvent_t> slab_events, packed_events, sent_events;
   cudaEvent_t ev_start = nullptr, ev_h2d = nullptr, ev_hash = nullptr, ev_exch = nullptr, ev_end = nullptr;
+  // Peer view mappings for the push exchange (CUDA IPC), re-validated on every load.
+  struct PeerView {
+    cudaIpcMemHandle_t handle{};
+    void* base = nullptr;  // mapped allocation base in this process
+    uint64_t offset = 0;   // view start inside the peer's allocation
+    uint64_t size = 0;     // peer's view bytes
+    bool open = false;
+  };
+  std::vector<PeerView> peer_views;
+  DevBuf ipc_records, barrier_word;
+  uint8_t* h_ipc = nullptr;  // pinned, world records
 };
 
 namespace {
@@ -144,6 +156,80 @@ tcx_status ensure_events(std::vector<cudaEvent_t>& v, uint64_t n) {
     cudaEvent_t e;
     TCX_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     v.push_back(e);
+  }
+  return TCX_OK;
+}
+
+// One rank's advertisement of its view buffer for the push exchange.
+struct IpcRecord {
+  cudaIpcMemHandle_t handle;  // 64 bytes: the allocation holding the view
+  uint64_t offset;            // view start inside that allocation
+  uint64_t size;              // view bytes
+  uint64_t valid;
+  uint64_t pad;
+};
+static_assert(sizeof(IpcRecord) == 96, "IPC record layout");
+
+// Stream-ordered barrier: completes on every rank only after every rank's earlier
+// work on its comm stream has completed.
+tcx_status nccl_barrier(tcx_group* g, Clock::time_point deadline) {
+  return nccl_check(g, ncclAllReduce(g->barrier_word.p, g->barrier_word.p, 1, ncclInt32, ncclSum, g->comm, g->s_comm),
+                    deadline, "barrier");
+}
+
+// Exchanges view handles (NCCL all-gather of one IpcRecord per rank) and maps every
+// peer's view into this process, reusing mappings whose handle has not changed.
+tcx_status map_peer_views(tcx_group* g, void* d_view, uint64_t view_bytes, Clock::time_point deadline) {
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  if (get_range == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    TCX_CUDA_TRY(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(TCX_UNAVAILABLE, "cuMemGetAddressRange is unavailable");
+    get_range = reinterpret_cast<GetRange>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t alloc = 0;
+  if (get_range(&base, &alloc, reinterpret_cast<CUdeviceptr>(d_view)) != CUDA_SUCCESS)
+    return set_error(TCX_INVALID_ARGUMENT, "d_view is not device memory this process allocated");
+  const uint64_t offset = reinterpret_cast<uint64_t>(d_view) - static_cast<uint64_t>(base);
+  if (offset + view_bytes > alloc) return set_error(TCX_INVALID_ARGUMENT, "view exceeds its allocation");
+  IpcRecord mine{};
+  TCX_CUDA_TRY(cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base)));
+  mine.offset = offset;
+  mine.size = view_bytes;
+  mine.valid = 1;
+  const uint64_t rec = sizeof(IpcRecord), world = static_cast<uint64_t>(g->world);
+  tcx_status st;
+  if ((st = g->ipc_records.grow((world + 1) * rec)) != TCX_OK) return st;
+  if (g->h_ipc == nullptr) TCX_CUDA_TRY(cudaMallocHost(&g->h_ipc, (world + 1) * rec));
+  std::memcpy(g->h_ipc + world * rec, &mine, rec);
+  TCX_CUDA_TRY(cudaMemcpyAsync(g->ipc_records.bytes() + world * rec, g->h_ipc + world * rec, rec,
+                               cudaMemcpyHostToDevice, g->s_comm));
+  st = nccl_check(g, ncclAllGather(g->ipc_records.bytes() + world * rec, g->ipc_records.p, rec, ncclUint8, g->comm,
+                                   g->s_comm), deadline, "view handle exchange");
+  if (st != TCX_OK) return st;
+  TCX_CUDA_TRY(cudaMemcpyAsync(g->h_ipc, g->ipc_records.p, world * rec, cudaMemcpyDeviceToHost, g->s_comm));
+  TCX_CUDA_TRY(cudaEventRecord(g->ev_exch, g->s_comm));
+  if ((st = wait_event(g, g->ev_exch, deadline)) != TCX_OK) return st;
+  g->peer_views.resize(world);
+  for (int p = 0; p < g->world; ++p) {
+    if (p == g->rank) continue;
+    IpcRecord r;
+    std::memcpy(&r, g->h_ipc + static_cast<uint64_t>(p) * rec, rec);
+    if (!r.valid) return set_errorf(TCX_INTERNAL, "rank %d sent no view handle", p);
+    auto& pv = g->peer_views[p];
+    if (!pv.open || std::memcmp(&pv.handle, &r.handle, sizeof r.handle) != 0) {
+      if (pv.open) cudaIpcCloseMemHandle(pv.base);
+      pv.open = false;
+      TCX_CUDA_TRY(cudaIpcOpenMemHandle(&pv.base, r.handle, cudaIpcMemLazyEnablePeerAccess));
+      pv.handle = r.handle;
+      pv.open = true;
+    }
+    pv.offset = r.offset;
+    pv.size = r.size;
   }
   return TCX_OK;
 }
@@ -227,6 +313,12 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   for (DevBuf* b : {&g->digests_mine, &g->states, &g->digests_all, &g->digests_compact, &g->merkle_scratch, &g->root,
                     &g->send, &g->recv, &g->perm_scratch, &g->jobs, &g->prefix, &g->view_digests, &g->view_scratch})
     b->release();
+  g->peer_views.clear();
+  for (auto& pv : g->peer_views)
+    if (pv.open) cudaIpcCloseMemHandle(pv.base);
+  g->ipc_records.release();
+  g->barrier_word.release();
+  if (g->h_ipc) cudaFreeHost(g->h_ipc);
   if (g->h_root) cudaFreeHost(g->h_root);
   if (g->h_jobs) cudaFreeHost(g->h_jobs);
   for (auto* v : {&g->slab_events, &g->packed_events, &g->sent_events})
@@ -415,9 +507,36 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     scat_off[k + 1] = round_scatter.size();
   }
 
+  // Push exchange: this rank writes each peer's view pieces from its staged range
+  // straight into the peer's view over NVLink (no pack or receive buffers).
+  const bool push = world > 1 && (plan->flags & TCX_LOAD_PEER_PUSH) != 0;
+  std::vector<tcx_copy_job> push_jobs;
+  std::vector<uint64_t> push_off(world + 1, 0);
+  uint64_t push_bytes = 0;
+  if (push) {
+    rounds = 0;
+    round_pack.clear();
+    round_scatter.clear();
+    std::fill(pack_off.begin(), pack_off.end(), 0);
+    std::fill(scat_off.begin(), scat_off.end(), 0);
+    for (int p = 0; p < world; ++p) {
+      push_off[p] = push_jobs.size();
+      if (p == rank) continue;
+      tmp.clear();
+      clip_jobs(plan->jobs + plan->job_offsets[p], plan->job_offsets[p + 1] - plan->job_offsets[p], lo, hi, tmp);
+      for (auto j : tmp) {
+        j.src_off -= lo;
+        push_bytes += j.rows * j.row_bytes;
+        push_jobs.push_back(j);
+      }
+    }
+    push_off[world] = push_jobs.size();
+  }
+
   // --- buffers --------------------------------------------------------------
-  const uint64_t n_jobs_all = round_pack.size() + local_kept.size() + round_scatter.size() + compact.size();
-  const uint64_t n_launches = 2 * rounds + 2;
+  const uint64_t n_jobs_all =
+      round_pack.size() + local_kept.size() + round_scatter.size() + compact.size() + push_jobs.size();
+  const uint64_t n_launches = 2 * rounds + 2 + static_cast<uint64_t>(world);
   if ((st = g->digests_mine.grow(std::max<uint64_t>(max_n, 1) * 32)) != TCX_OK) return st;
   if ((st = g->states.grow(std::max<uint64_t>(n_mine, 1) * 32)) != TCX_OK) return st;
   if ((st = g->merkle_scratch.grow(merkle_scratch_bytes(n_total))) != TCX_OK) return st;
@@ -427,6 +546,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   if (rounds && max_send && (st = g->send.grow(2 * peers.size() * send_slot)) != TCX_OK) return st;
   if (rounds && max_recv_buf && (st = g->recv.grow(2 * peers.size() * recv_slot)) != TCX_OK) return st;
   if (perm_bytes && (st = g->perm_scratch.grow(perm_bytes)) != TCX_OK) return st;
+  if (push && (st = g->barrier_word.grow(256)) != TCX_OK) return st;
   if (world > 1) {
     if ((st = g->digests_all.grow(static_cast<uint64_t>(world) * max_n * 32)) != TCX_OK) return st;
     if ((st = g->digests_compact.grow(n_total * 32)) != TCX_OK) return st;
@@ -450,11 +570,12 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   }
   tcx_copy_job* hj = g->h_jobs;
   const uint64_t o_pack = 0, o_local = round_pack.size(), o_scatter = o_local + local_kept.size(),
-                 o_compact = o_scatter + round_scatter.size();
+                 o_compact = o_scatter + round_scatter.size(), o_push = o_compact + compact.size();
   std::copy(round_pack.begin(), round_pack.end(), hj + o_pack);
   std::copy(local_kept.begin(), local_kept.end(), hj + o_local);
   std::copy(round_scatter.begin(), round_scatter.end(), hj + o_scatter);
   std::copy(compact.begin(), compact.end(), hj + o_compact);
+  std::copy(push_jobs.begin(), push_jobs.end(), hj + o_push);
   auto* dj = static_cast<tcx_copy_job*>(g->jobs.p);
   auto* dprefix = static_cast<uint64_t*>(g->prefix.p);
   // Each copy-job launch gets its own prefix region, handed out in launch order
@@ -470,6 +591,20 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   const auto* hstage = static_cast<const uint8_t*>(h_stage);
 
   const auto deadline = Clock::now() + std::chrono::milliseconds(g->timeout_ms);
+  if (push) {
+    // Map every peer's view (collective) and check that each push stays inside it.
+    if ((st = map_peer_views(g, d_view, plan->view_bytes, deadline)) != TCX_OK) return st;
+    for (int p = 0; p < world; ++p) {
+      if (p == rank) continue;
+      for (uint64_t i = push_off[p]; i < push_off[p + 1]; ++i) {
+        const tcx_copy_job& j = push_jobs[i];
+        const uint64_t end = j.dst_off + (j.rows - 1) * j.dst_pitch + j.row_bytes;
+        if (end > g->peer_views[p].size)
+          return set_errorf(TCX_INVALID_ARGUMENT, "rank %d's view (%llu bytes) is smaller than its jobs need", p,
+                            static_cast<unsigned long long>(g->peer_views[p].size));
+      }
+    }
+  }
 
   // --- H2D + hashing ---------------------------------------------------------
   // Everything queued on the caller's stream before this call (writes into the
@@ -526,6 +661,22 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
       (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), g->s_comm)) != TCX_OK)
     return st;
   uint64_t sent = 0, received = 0;
+  if (push) {
+    // Every rank's view is ready to be written (its gaps cleared, its earlier loads done).
+    if ((st = nccl_barrier(g, deadline)) != TCX_OK) return st;
+    for (int p = 0; p < world; ++p) {
+      const uint64_t n = push_off[p + 1] - push_off[p];
+      if (p == rank || n == 0) continue;
+      uint8_t* peer_view = static_cast<uint8_t*>(g->peer_views[p].base) + g->peer_views[p].offset;
+      if ((st = launch_copy_jobs(stage, peer_view, dj + o_push + push_off[p], n, prefix_for(n), g->s_comm)) != TCX_OK)
+        return st;
+    }
+    // Every peer has finished writing into this rank's view.
+    if ((st = nccl_barrier(g, deadline)) != TCX_OK) return st;
+    sent = push_bytes;
+    for (int p = 0; p < world; ++p)
+      if (p != rank) received += recv_counts[p];
+  }
   for (uint64_t k = 0; k < rounds; ++k) {
     const uint64_t buf = k % 2;
     // pack round k on the pack stream once round k-2 (same buffer) has been sent

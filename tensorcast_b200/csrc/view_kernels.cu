@@ -124,6 +124,9 @@ __global__ void __launch_bounds__(kCopyThreads) copy_jobs_kernel(const uint8_t* 
       }
     }
   }
+  // Destinations may be a peer GPU's memory: make the writes visible system-wide
+  // before the kernel ends (a later barrier then orders them for the peer).
+  __threadfence_system();
 }
 
 // ---------------------------------------------------------------------------

@@ -19,6 +19,7 @@ from .views import JOB_DTYPE, permute_array
 
 
 VIEW_HASH = 1  # TCX_LOAD_VIEW_HASH
+PEER_PUSH = 2  # TCX_LOAD_PEER_PUSH
 
 
 def stage_bounds(total: int, leaf: int, world: int) -> list[int]:
@@ -158,12 +159,14 @@ class Group:
 
     def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, permutes=(), view_bytes=None,
              expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0,
-             view_hash: bool = False) -> dict:
+             view_hash: bool = False, peer_push: bool = False) -> dict:
+        """peer_push: exchange by writing into the peers' views over NVLink (d_view must be a
+        cudaMalloc allocation of this process, e.g. a torch CUDA tensor); else NCCL send/recv."""
         """Runs one load; returns the result fields as a dict. h_stage None: device-resident."""
         if view_bytes is None:
             view_bytes = d_view.numel() * d_view.element_size() if isinstance(d_view, torch.Tensor) else 0
         plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes, window_bytes,
-                     flags=VIEW_HASH if view_hash else 0)
+                     flags=(VIEW_HASH if view_hash else 0) | (PEER_PUSH if peer_push else 0))
         res = _native.LoadResult()
         exp = None
         if expected_root is not None:

@@ -25,6 +25,7 @@ def to_dev(a: np.ndarray, offset: int = 0) -> torch.Tensor:
     """Device copy of a at byte offset `offset` inside a larger allocation."""
     buf = torch.zeros(a.size + offset + 64, dtype=torch.uint8, device="cuda")
     buf[offset:offset + a.size] = torch.from_numpy(a).cuda()
+    torch.cuda.synchronize()
     return buf[offset:offset + a.size]
 
 

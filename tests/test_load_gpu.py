@@ -18,7 +18,9 @@ pytestmark = pytest.mark.gpu
 
 
 def dev(a: np.ndarray) -> torch.Tensor:
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    torch.cuda.synchronize()
+    return t
 
 
 def pinned(a: np.ndarray) -> torch.Tensor:
