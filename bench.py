@@ -134,10 +134,13 @@ def run_copy_only(args) -> None:
                                         scratch.data_ptr(), sb, s.cuda_stream))
         res[name] = {"bytes_moved": 2 * nbytes, "ms": round(ms, 4), "gbs": round(2 * nbytes / ms / 1e6, 1)}
     out = torch.empty_like(src)
-    pj = _native.PermuteJob(0, 0, es, 2)
-    pj.shape[0], pj.shape[1], pj.perm[0], pj.perm[1] = rows, cols, 1, 0
-    ms = timed(lambda: _native.call("tcx_permute", src.data_ptr(), out.data_ptr(), ctypes.byref(pj), s.cuda_stream))
-    res["transpose"] = {"bytes_moved": 2 * src.numel(), "ms": round(ms, 4), "gbs": round(2 * src.numel() / ms / 1e6, 1)}
+    # the same bytes as [rows, cols] bf16, [rows, 2*cols] 1-byte and [rows, cols/2] 4-byte elements
+    for key, esize, ncols in (("transpose", es, cols), ("transpose_1byte", 1, cols * es),
+                              ("transpose_4byte", 4, cols * es // 4)):
+        pj = _native.PermuteJob(0, 0, esize, 2)
+        pj.shape[0], pj.shape[1], pj.perm[0], pj.perm[1] = rows, ncols, 1, 0
+        ms = timed(lambda: _native.call("tcx_permute", src.data_ptr(), out.data_ptr(), ctypes.byref(pj), s.cuda_stream))
+        res[key] = {"bytes_moved": 2 * src.numel(), "ms": round(ms, 4), "gbs": round(2 * src.numel() / ms / 1e6, 1)}
     res["hbm_gbs"] = measured_hbm()
     print(json.dumps(res), flush=True)
 
@@ -708,8 +711,11 @@ def hash_kernel_roofline(d_stage, nbytes: int, leaf: int, rank: int) -> dict:
     pout = torch.empty((probe_n, 32), dtype=torch.uint8, device="cuda")
     pms = timed(lambda: _native.call("tcx_sha256_compute_probe", probe_n, probe_b, pout.data_ptr(), s.cuda_stream))
     compute = probe_n * probe_b * 64 / pms / 1e6
-    # Chain latency: one warp, 4096 blocks.
-    lms = timed(lambda: _native.call("tcx_sha256_compute_probe", 32, 4096, pout.data_ptr(), s.cuda_stream), reps=2)
+    # Chain latency of the leaf kernel itself: 32 chains (one consumer warp) of 4096 blocks each.
+    lb = 4096 * 64
+    lout = torch.empty((32, 32), dtype=torch.uint8, device="cuda")
+    lsrc = d_stage[: 32 * lb] if d_stage.numel() >= 32 * lb else torch.zeros(32 * lb, dtype=torch.uint8, device="cuda")
+    lms = timed(lambda: tcx.sha256_leaves(lsrc, lb, lout, nbytes=32 * lb - 64, stream=s), reps=2)
     t_block_us = lms * 1e3 / 4096
     chain = n * 64 / (t_block_us * 1e-6) / 1e9
     hbm = measured_hbm()
@@ -722,7 +728,7 @@ def hash_kernel_roofline(d_stage, nbytes: int, leaf: int, rank: int) -> dict:
             "compute_bound_gbs": round(compute, 2), "compute_bound_source": "measured: register-only SHA-256 probe, "
             f"{probe_n} chains x {probe_b} blocks", "hbm_gbs": hbm["gbs"], "hbm_source": hbm["source"],
             "frac_of_hbm": round(achieved / hbm["gbs"], 4), "chain_bound_gbs": round(chain, 2),
-            "t_block_us_single_warp": round(t_block_us, 4), "frac_of_chain_bound": round(achieved / chain, 4)}
+            "t_block_us_one_chain_per_lane": round(t_block_us, 4), "frac_of_chain_bound": round(achieved / chain, 4)}
 
 
 def measured_hbm() -> dict:

@@ -668,7 +668,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
       const uint64_t n = push_off[p + 1] - push_off[p];
       if (p == rank || n == 0) continue;
       uint8_t* peer_view = static_cast<uint8_t*>(g->peer_views[p].base) + g->peer_views[p].offset;
-      if ((st = launch_copy_jobs(stage, peer_view, dj + o_push + push_off[p], n, prefix_for(n), g->s_comm)) != TCX_OK)
+      if ((st = launch_copy_jobs(stage, peer_view, dj + o_push + push_off[p], n, prefix_for(n), g->s_comm, true)) != TCX_OK)
         return st;
     }
     // Every peer has finished writing into this rank's view.

@@ -22,8 +22,9 @@ void clear_error();
 void note_launches(uint64_t n);
 
 // Kernel launchers shared between translation units (stream-ordered).
+// remote_dst: d_dst is a peer GPU's memory (the kernel ends with a system-scope fence).
 tcx_status launch_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* d_jobs, uint64_t n_jobs,
-                            uint64_t* d_prefix, cudaStream_t stream);
+                            uint64_t* d_prefix, cudaStream_t stream, bool remote_dst = false);
 tcx_status launch_permute(const void* d_src, void* d_dst, const tcx_permute_job& pj, cudaStream_t stream);
 tcx_status check_permute(const tcx_permute_job& pj);
 tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, uint64_t seg_off,

@@ -15,9 +15,10 @@
 // Rows are moved as 16-byte vectors when every offset, pitch and length of the
 // job is 16-byte aligned, otherwise byte by byte.
 //
-// permute_kernel transposes 2-D tensors through 64x64-element shared-memory
-// tiles (16-byte global accesses on both sides); other permutations use a
-// generic gather.
+// 2-D transposes of 1- and 2-byte elements go through transpose2d_packed_kernel
+// (element blocks transposed in registers into 32-bit words, a swizzled word
+// tile, 16-byte global accesses on both sides), 4- and 8-byte elements through
+// 64x64-element padded tiles; other permutations use a generic gather.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -72,7 +73,8 @@ __device__ __forceinline__ uint64_t find_job(const uint64_t* prefix, uint64_t n,
 __global__ void __launch_bounds__(kCopyThreads) copy_jobs_kernel(const uint8_t* __restrict__ src,
                                                                  uint8_t* __restrict__ dst,
                                                                  const tcx_copy_job* __restrict__ jobs, uint64_t n,
-                                                                 const uint64_t* __restrict__ prefix) {
+                                                                 const uint64_t* __restrict__ prefix,
+                                                                 bool remote_dst) {
   __shared__ uint64_t s_job;
   const uint64_t total = prefix[n];
   for (uint64_t w = blockIdx.x; w < total; w += gridDim.x) {
@@ -124,9 +126,14 @@ __global__ void __launch_bounds__(kCopyThreads) copy_jobs_kernel(const uint8_t* 
       }
     }
   }
-  // Destinations may be a peer GPU's memory: make the writes visible system-wide
-  // before the kernel ends (a later barrier then orders them for the peer).
-  __threadfence_system();
+  // A destination in a peer GPU's memory: after the CTA's barrier one thread's
+  // system-scope fence (cumulative over the writes the barrier ordered before it)
+  // makes the CTA's stores visible to the peer before the kernel ends; the
+  // barrier that follows on the host side then orders them for the peer.
+  if (remote_dst) {
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -180,6 +187,104 @@ __global__ void __launch_bounds__(256) transpose2d_kernel(const T* __restrict__ 
   }
 }
 
+// Packed-word transpose for 1- and 2-byte elements (P = 4 or 2 elements per
+// 32-bit word). A tile is 32*P source rows by 32*P source columns: 32 row
+// groups of P rows, each source row segment 128 bytes (8 chunks of 16 bytes).
+// Phase 1: thread (group g, chunk q) loads the chunk from the P rows of its
+// group (P 16-byte loads) and transposes them in registers with byte permutes
+// into 4*P words, word j = the P elements of source column j, one per row, in
+// row order, i.e. P consecutive elements of output row j. Words land in a
+// shared tile W[column][group] whose group index is XOR-swizzled by 4*(chunk)
+// so the 32 lanes of a store hit 32 distinct banks.
+// Phase 2: each 16-byte output chunk (4 consecutive groups) is one swizzled,
+// 16-byte-aligned shared load and one 16-byte global store; 8 lanes cover 128
+// contiguous bytes of an output row.
+// Full tiles only, and only when every row start is 16-byte aligned on both
+// sides; edge tiles copy element by element.
+template <int P>
+struct PackedElem;
+template <>
+struct PackedElem<2> {
+  using T = uint16_t;
+};
+template <>
+struct PackedElem<4> {
+  using T = uint8_t;
+};
+
+template <int P>
+__device__ __forceinline__ void transpose_words(const uint32_t (&in)[P], uint32_t (&out)[P]);
+
+template <>
+__device__ __forceinline__ void transpose_words<2>(const uint32_t (&in)[2], uint32_t (&out)[2]) {
+  out[0] = __byte_perm(in[0], in[1], 0x5410);  // low halves: element 0 of rows 0, 1
+  out[1] = __byte_perm(in[0], in[1], 0x7632);  // high halves: element 1 of rows 0, 1
+}
+
+template <>
+__device__ __forceinline__ void transpose_words<4>(const uint32_t (&in)[4], uint32_t (&out)[4]) {
+  const uint32_t t0 = __byte_perm(in[0], in[1], 0x5140);  // (r0.b0, r1.b0, r0.b1, r1.b1)
+  const uint32_t t1 = __byte_perm(in[2], in[3], 0x5140);  // (r2.b0, r3.b0, r2.b1, r3.b1)
+  const uint32_t t2 = __byte_perm(in[0], in[1], 0x7362);  // (r0.b2, r1.b2, r0.b3, r1.b3)
+  const uint32_t t3 = __byte_perm(in[2], in[3], 0x7362);  // (r2.b2, r3.b2, r2.b3, r3.b3)
+  out[0] = __byte_perm(t0, t1, 0x5410);
+  out[1] = __byte_perm(t0, t1, 0x7632);
+  out[2] = __byte_perm(t2, t3, 0x5410);
+  out[3] = __byte_perm(t2, t3, 0x7632);
+}
+
+template <int P, int G>
+__global__ void __launch_bounds__(256) transpose2d_packed_kernel(const typename PackedElem<P>::T* __restrict__ src,
+                                                                 typename PackedElem<P>::T* __restrict__ dst,
+                                                                 uint64_t rows, uint64_t cols, bool vec) {
+  using T = typename PackedElem<P>::T;
+  constexpr int TR = 32 * P;      // source rows of one tile
+  constexpr int R = TR * G;       // a CTA takes G tiles stacked along the rows
+  constexpr int C = 32 * P;       // source columns of a tile
+  constexpr int CPQ = 4 * P;      // columns per 16-byte chunk
+  __shared__ __align__(16) uint32_t W[G][C][32];
+  const uint64_t tiles_c = (cols + C - 1) / C;
+  const uint64_t tr = blockIdx.x / tiles_c, tc = blockIdx.x % tiles_c;
+  const uint64_t r0 = tr * R, c0 = tc * C;
+  if (vec && r0 + R <= rows && c0 + C <= cols) {
+    const int q = threadIdx.x & 7, g = threadIdx.x >> 3;
+    uint4 v[G][P];  // every load of the CTA's tiles in flight before the first shared store
+#pragma unroll
+    for (int t = 0; t < G; ++t)
+#pragma unroll
+      for (int k = 0; k < P; ++k)
+        v[t][k] = *reinterpret_cast<const uint4*>(src + (r0 + t * TR + P * g + k) * cols + c0 + q * CPQ);
+    const int phys = g ^ (4 * q);
+#pragma unroll
+    for (int t = 0; t < G; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t in[P], out[P];
+#pragma unroll
+        for (int k = 0; k < P; ++k) in[k] = reinterpret_cast<const uint32_t*>(&v[t][k])[i];
+        transpose_words<P>(in, out);
+#pragma unroll
+        for (int k = 0; k < P; ++k) W[t][q * CPQ + i * P + k][phys] = out[k];
+      }
+    __syncthreads();
+    // item m: output row j, tile t, chunk c; 8*G consecutive lanes cover G*128
+    // contiguous bytes of one output row.
+#pragma unroll
+    for (int m = threadIdx.x; m < G * C * 8; m += 256) {
+      const int c = m & 7, t = (m >> 3) % G, j = (m >> 3) / G;
+      const uint4 o = *reinterpret_cast<const uint4*>(&W[t][j][4 * (c ^ ((j / CPQ) & 7))]);
+      *reinterpret_cast<uint4*>(dst + (c0 + j) * rows + r0 + t * TR + c * CPQ) = o;
+    }
+  } else {
+    const uint64_t nr = rows - r0 < static_cast<uint64_t>(R) ? rows - r0 : R;
+    const uint64_t nc = cols - c0 < static_cast<uint64_t>(C) ? cols - c0 : C;
+    for (uint64_t k = threadIdx.x; k < nr * nc; k += blockDim.x) {
+      const uint64_t j = k / nr, r = k % nr;
+      dst[(c0 + j) * rows + r0 + r] = src[(r0 + r) * cols + c0 + j];
+    }
+  }
+}
+
 struct PermuteParams {
   uint32_t ndim;
   uint64_t out_shape[TCX_MAX_DIMS];
@@ -223,9 +328,17 @@ tcx_status launch_permute_t(const uint8_t* src, uint8_t* dst, const tcx_permute_
     const uint64_t rows = pj.shape[0], cols = pj.shape[1];
     const bool vec = ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(o)) & 15u) == 0 &&
                      (rows * sizeof(T)) % 16 == 0 && (cols * sizeof(T)) % 16 == 0;
-    const uint64_t tiles = ((rows + kTile - 1) / kTile) * ((cols + kTile - 1) / kTile);
-    if (tiles > 0x7fffffffull) return set_error(TCX_INVALID_ARGUMENT, "tensor too large to permute");
-    transpose2d_kernel<T><<<static_cast<unsigned>(tiles), 256, 0, stream>>>(s, o, rows, cols, vec);
+    if constexpr (sizeof(T) <= 2) {
+      // 16 KiB of loads in flight per CTA: two 64x64 tiles of 2-byte elements, one 128x128 of 1-byte.
+      constexpr int P = 4 / sizeof(T), G = P == 2 ? 2 : 1, E = 32 * P;
+      const uint64_t tiles = ((rows + E * G - 1) / (E * G)) * ((cols + E - 1) / E);
+      if (tiles > 0x7fffffffull) return set_error(TCX_INVALID_ARGUMENT, "tensor too large to permute");
+      transpose2d_packed_kernel<P, G><<<static_cast<unsigned>(tiles), 256, 0, stream>>>(s, o, rows, cols, vec);
+    } else {
+      const uint64_t tiles = ((rows + kTile - 1) / kTile) * ((cols + kTile - 1) / kTile);
+      if (tiles > 0x7fffffffull) return set_error(TCX_INVALID_ARGUMENT, "tensor too large to permute");
+      transpose2d_kernel<T><<<static_cast<unsigned>(tiles), 256, 0, stream>>>(s, o, rows, cols, vec);
+    }
     note_launches(1);
   } else {
     PermuteParams pp{};
@@ -251,14 +364,14 @@ tcx_status launch_permute_t(const uint8_t* src, uint8_t* dst, const tcx_permute_
 }  // namespace
 
 tcx_status launch_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* d_jobs, uint64_t n_jobs,
-                            uint64_t* d_prefix, cudaStream_t stream) {
+                            uint64_t* d_prefix, cudaStream_t stream, bool remote_dst) {
   if (n_jobs == 0) return TCX_OK;
   copy_prefix_kernel<<<1, 1024, 0, stream>>>(d_jobs, n_jobs, d_prefix);
   note_launches(1);
   TCX_CUDA_TRY(cudaGetLastError());
   const unsigned grid = static_cast<unsigned>(sm_count()) * 8u;
   copy_jobs_kernel<<<grid, kCopyThreads, 0, stream>>>(static_cast<const uint8_t*>(d_src),
-                                                      static_cast<uint8_t*>(d_dst), d_jobs, n_jobs, d_prefix);
+                                                      static_cast<uint8_t*>(d_dst), d_jobs, n_jobs, d_prefix, remote_dst);
   note_launches(1);
   TCX_CUDA_TRY(cudaGetLastError());
   return TCX_OK;

@@ -60,14 +60,20 @@ def test_copy_jobs_and_permutes_match_oracle(cuda_device):
         assert (view.cpu().numpy()[: plan.view_bytes] == want).all()
 
 
-@pytest.mark.parametrize("rows,cols", [(64, 64), (4096, 1024), (130, 77), (8192, 8192), (1, 640), (640, 1)])
-def test_transpose_bf16_shapes(cuda_device, rows, cols):
-    a = np.random.default_rng(rows + cols).integers(0, 65536, size=(rows, cols), dtype=np.uint16)
-    src, out = dev(a.view(np.uint8).reshape(-1)), torch.empty(a.size * 2, dtype=torch.uint8, device="cuda")
-    pj = _native.PermuteJob(0, 0, 2, 2)
+@pytest.mark.parametrize("esize", [2, 1, 4, 8])
+@pytest.mark.parametrize("rows,cols", [(64, 64), (4096, 1024), (130, 77), (8192, 8192), (1, 640), (640, 1),
+                                       (200, 136), (256, 144), (136, 4096)])
+def test_transpose_shapes(cuda_device, rows, cols, esize):
+    """2-D transposes: full and edge tiles, aligned (16-byte rows) and unaligned shapes."""
+    dt = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}[esize]
+    if esize == 8 and rows * cols > 1 << 24:
+        pytest.skip("large 8-byte case adds nothing over the 2-byte one")
+    a = np.random.default_rng(rows + cols).integers(0, np.iinfo(dt).max, size=(rows, cols), dtype=dt)
+    src, out = dev(a.view(np.uint8).reshape(-1)), torch.empty(a.size * esize, dtype=torch.uint8, device="cuda")
+    pj = _native.PermuteJob(0, 0, esize, 2)
     pj.shape[0], pj.shape[1], pj.perm[0], pj.perm[1] = rows, cols, 1, 0
     _native.call("tcx_permute", src.data_ptr(), out.data_ptr(), ctypes.byref(pj), torch.cuda.current_stream().cuda_stream)
-    assert (out.cpu().numpy().view(np.uint16).reshape(cols, rows) == a.T).all()
+    assert (out.cpu().numpy().view(dt).reshape(cols, rows) == a.T).all()
 
 
 def test_streamed_passes_match_single_pass(cuda_device):
