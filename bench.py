@@ -37,7 +37,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Realized GB/s into 1/2/4/8 B200 (SHA-256 verified); GPU SHA-256 GB/s/GPU"
 LEAF = 4 << 20
-SEED = 1
+SEEDS = {"llama3-8b": 1, "llama3-70b": 2}  # BASELINE configs 2 and 4
 
 
 def parse_args():
@@ -57,9 +57,11 @@ def parse_args():
     ap.add_argument("--stage", choices=["mapped", "pinned"], default="pinned",
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
                          "(no second host copy), or a pinned copy read with parallel preads")
-    ap.add_argument("--workload", choices=["artifact", "kv"], default="artifact",
+    ap.add_argument("--workload", choices=["artifact", "kv", "disk-hash"], default="artifact",
                     help="artifact: the collective from-disk load (default); kv: BASELINE config 5, paged KV "
-                         "gather + per-sequence hash, 8 sequence shards dealt to the ranks")
+                         "gather + per-sequence hash, 8 sequence shards dealt to the ranks; disk-hash: "
+                         "compute_data_multihash_from_disk_dir of the artifact's directory on one GPU, against "
+                         "the reference's single-core CPU path")
     ap.add_argument("--copy-only", metavar="ROWS:COLS:TP",
                     help="only time the view kernels on a bf16 [ROWS, COLS] tensor: the dim-0 and dim-1 "
                          "tensor-parallel shards of rank 0 of TP (copy jobs) and a full transpose")
@@ -153,7 +155,7 @@ def log(*a):
 # Artifact
 # ---------------------------------------------------------------------------
 def artifact_path(args) -> str:
-    return os.path.join(args.dir, f"{args.model}-seed{SEED}.safetensors")
+    return os.path.join(args.dir, f"{args.model}-seed{SEEDS[args.model]}.safetensors")
 
 
 TRANSPOSED_O_PROJ = "model.layers.0.self_attn.o_proj.weight"
@@ -187,9 +189,9 @@ def ensure_artifact(args, rank: int, local_rank: int, world: int = 1) -> str:
         t0 = time.time()
         dev = f"cuda:{local_rank}" if torch.cuda.is_available() else "cpu"
         if world > 1:
-            info = write_safetensors_parallel(path, shapes, SEED, world, rank, device=dev)
+            info = write_safetensors_parallel(path, shapes, SEEDS[args.model], world, rank, device=dev)
         else:
-            info = write_safetensors(path, shapes, SEED, device=dev)
+            info = write_safetensors(path, shapes, SEEDS[args.model], device=dev)
         if rank == 0:
             with open(marker, "w") as f:
                 json.dump(info, f)
@@ -307,6 +309,52 @@ def cpu_reference_sample(path: str, payload_off: int, total: int, leaf: int, tar
             "seconds": round(dt, 2), "host_nproc": os.cpu_count()}
 
 
+def run_disk_hash(args) -> None:
+    """compute_data_multihash_from_disk_dir (disk_dir_hash.cc:47-104) of a directory holding
+    the artifact: preads into pinned slots, H2D and the leaf kernel per 1 GiB group of 4 MiB
+    leaves, Merkle root on the GPU; wall-clock timed (the call is synchronous), result
+    checked against the CPU oracle over the same payload bytes."""
+    import numpy as np
+    import torch
+    from oracle import oracle
+    from tensorcast_b200.disk_hash import compute_data_multihash_from_disk_dir
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    torch.cuda.set_device(0)
+    path = ensure_artifact(args, 0, 0)
+    d = os.path.join(args.dir, f"dirhash-{args.model}")
+    os.makedirs(d, exist_ok=True)
+    link = os.path.join(d, "model.safetensors")
+    if not os.path.islink(link):
+        os.symlink(path, link)
+    with open(path + ".done") as f:
+        info = json.load(f)
+    T = info["total_bytes"]
+    for _ in range(args.warmup):
+        got = compute_data_multihash_from_disk_dir(d)
+    times = []
+    with ClockSampler(0) as clocks:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            got = compute_data_multihash_from_disk_dir(d)
+            times.append(time.perf_counter() - t0)
+    raw = np.memmap(path, dtype=np.uint8, mode="r", offset=info["payload_offset"], shape=(T,))
+    want = oracle.multihash(oracle.tree_root(oracle.leaf_digests(raw, LEAF, openssl=True,
+                                                                    threads=min(32, os.cpu_count() or 1))))
+    ms = statistics.median(times) * 1e3
+    cpu = None if args.no_cpu_baseline else cpu_reference_sample(path, info["payload_offset"], T, LEAF,
+                                                                 args.cpu_seconds)
+    print(json.dumps({"metric": "compute_data_multihash_from_disk_dir GB/s (tmpfs -> GPU SHA-256)",
+                      "value": round(T / ms / 1e6, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": round(ms, 1), "higher_is_better": True,
+                      "config": {"workload": f"{args.model} safetensors directory, {T} B payload, 4 MiB leaves",
+                                 "timing": "wall clock of the synchronous call, page-cache-hot tmpfs"},
+                      "multihash": got, "matches_cpu_oracle": got == want, "cpu_baseline": cpu,
+                      "clocks": clocks.summary()}), flush=True)
+    if got != want:
+        raise SystemExit("disk-dir multihash differs from the CPU oracle")
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -349,6 +397,9 @@ def main() -> None:
         return
     if args.workload == "kv":
         run_kv(args)
+        return
+    if args.workload == "disk-hash":
+        run_disk_hash(args)
         return
     if args.impl == "reference":
         run_reference(args)
@@ -518,9 +569,9 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
             "config": {
-                "workload": (f"{args.model}-shaped bf16 safetensors (seed {SEED}), {T} B, identity view"
+                "workload": (f"{args.model}-shaped bf16 safetensors (seed {SEEDS[args.model]}), {T} B, identity view"
                              if world == 1 else
-                             f"{args.model}-shaped bf16 safetensors (seed {SEED}), {T} B, TP-{world} views "
+                             f"{args.model}-shaped bf16 safetensors (seed {SEEDS[args.model]}), {T} B, TP-{world} views "
                              f"(q/k/v/gate/up/embed/lm_head dim 0, o/down dim 1)"
                              + (f"; {transposed} stored [in, out] and read whole through a transpose view"
                                 if transposed else "")),

@@ -322,6 +322,36 @@ tcx_status tcx_plan_exchange(const tcx_load_plan* plan, int world, int rank, tcx
  * parallel preads; a short read is DATA_LOSS (source_hash.cc:44-51). */
 tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n, void* dst, int threads);
 
+/* Progress of a streamed hash: bytes whose leaves are hashed so far, of total. */
+typedef void (*tcx_progress_fn)(uint64_t processed_bytes, uint64_t total_bytes, void* ctx);
+
+/* Data multihash of a byte stream stored in files, hashed on `device`.
+ * Replaces compute_data_multihash_from_seekable_source
+ * (core/store/materialization/dataplane/metadata/source_hash.cc:19-61) as
+ * called by compute_data_multihash_from_disk_dir (disk_dir_hash.cc:47-104):
+ * the stream [0, total) is given as file segments in stream order (dst_offset
+ * = stream offset; they must tile [0, total) exactly), cut into leaves of
+ * leaf_bytes (used as given, no adaptive policy, as the CPU path), SHA-256 per
+ * leaf, Merkle tree, multihash. Groups of whole leaves (group_bytes, 0 = 1 GiB)
+ * are read by read_threads parallel preads (0 = up to 16) into `depth` pinned
+ * slots (0 = 4), copied to the device and hashed on one stream per slot, so
+ * reads, copies and hashing overlap. The slots stay allocated per device for
+ * the next call (tcx_file_hash_release frees them); calls on one device are
+ * serialised. Synchronous; restores the caller's current device. Errors as
+ * the reference: total 0 or leaf 0 is
+ * INVALID_ARGUMENT, a short read DATA_LOSS "short read while hashing source".
+ * root_out (optional) receives the 32-byte root; out (>= 57 bytes) the
+ * multihash. progress (optional) is called on the calling thread. */
+tcx_status tcx_multihash_from_file_segments(const tcx_file_segment* segs, uint64_t n_segs, uint64_t total,
+                                            uint64_t leaf_bytes, int device, uint64_t group_bytes, int depth,
+                                            int read_threads, tcx_progress_fn progress, void* progress_ctx,
+                                            uint8_t* root_out, char* out, uint64_t out_len);
+
+/* Frees the pinned and device buffers tcx_multihash_from_file_segments keeps for
+ * `device` (-1: every device). No counterpart in the reference (it allocates per
+ * call). */
+tcx_status tcx_file_hash_release(int device);
+
 /* Maps [offset, offset + length) of a file into host memory and, when
  * register_pinned != 0, page-locks the mapping (cudaHostRegister; a read-only
  * mapping registered read-only where the driver accepts it, else a shared

@@ -1,0 +1,269 @@
+// Data multihash of byte ranges of files, hashed on the GPU.
+//
+// The reference hashes an artifact directory on the CPU
+// (compute_data_multihash_from_disk_dir, disk_dir_hash.cc:47-104, through
+// compute_data_multihash_from_seekable_source, source_hash.cc:19-61): the
+// files' bytes form one stream (safetensors payloads in file-name order, or
+// numbered partitions in numeric order), cut into fixed leaves, one SHA-256
+// per leaf on one core, then the Merkle tree. Here the caller resolves the
+// stream to file segments and this entry point streams it through the GPU:
+//
+//   host threads: pread group k+1 into pinned slot (k+1) % depth
+//   slot stream:  H2D of group k, then the leaf kernel over its whole leaves
+//   end:          Merkle root of all leaf digests on the device, 32 bytes back
+//
+// A group is a whole number of leaves, so every leaf is hashed in one launch
+// and groups are independent; `depth` slots (pinned + device buffer + stream)
+// keep reads, copies and hashing of different groups in flight at once. The
+// slots stay allocated per device between calls (tcx_file_hash_release frees
+// them); calls on one device are serialised.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "tcx_internal.h"
+
+namespace tcx {
+namespace {
+
+constexpr uint64_t kDefaultGroupBytes = 1ull << 30;
+constexpr int kDefaultDepth = 4;
+
+struct Slot {
+  uint8_t* host = nullptr;
+  uint8_t* dev = nullptr;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t hashed = nullptr;  // leaf digests of the slot's group written
+  int64_t group = -1;
+};
+
+// Per-device buffers, kept between calls (page-locking gigabytes of host memory
+// costs far more than one hash of them) until tcx_file_hash_release.
+struct FileHashContext {
+  std::mutex mu;
+  std::vector<Slot> slots;
+  uint64_t slot_bytes = 0;
+  uint8_t* digests = nullptr;
+  uint64_t digest_bytes = 0;
+  uint8_t* scratch = nullptr;
+  uint64_t scratch_bytes = 0;
+  uint8_t* root = nullptr;
+
+  void free_slots() {
+    for (auto& s : slots) {
+      if (s.stream) cudaStreamSynchronize(s.stream);
+      if (s.hashed) cudaEventDestroy(s.hashed);
+      if (s.stream) cudaStreamDestroy(s.stream);
+      if (s.host) cudaFreeHost(s.host);
+      if (s.dev) cudaFree(s.dev);
+    }
+    slots.clear();
+    slot_bytes = 0;
+  }
+  void free_all() {
+    free_slots();
+    if (digests) cudaFree(digests);
+    if (scratch) cudaFree(scratch);
+    if (root) cudaFree(root);
+    digests = scratch = root = nullptr;
+    digest_bytes = scratch_bytes = 0;
+  }
+  tcx_status ensure(int n_slots, uint64_t bytes, uint64_t n_digest_bytes, uint64_t n_scratch_bytes) {
+    if (static_cast<int>(slots.size()) < n_slots || slot_bytes < bytes) {
+      free_slots();
+      slots.resize(n_slots);
+      slot_bytes = bytes;
+      for (auto& s : slots) {
+        cudaError_t e = cudaMallocHost(&s.host, bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&s.dev, bytes);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.hashed, cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+          free_slots();
+          return set_error(e == cudaErrorMemoryAllocation ? TCX_RESOURCE_EXHAUSTED : TCX_INTERNAL,
+                           std::string("file hash buffers: ") + cudaGetErrorString(e));
+        }
+      }
+    }
+    for (auto& s : slots) s.group = -1;
+    if (digest_bytes < n_digest_bytes) {
+      if (digests) cudaFree(digests);
+      digests = nullptr;
+      digest_bytes = 0;
+      TCX_CUDA_TRY(cudaMalloc(&digests, n_digest_bytes));
+      digest_bytes = n_digest_bytes;
+    }
+    if (scratch_bytes < n_scratch_bytes) {
+      if (scratch) cudaFree(scratch);
+      scratch = nullptr;
+      scratch_bytes = 0;
+      TCX_CUDA_TRY(cudaMalloc(&scratch, n_scratch_bytes));
+      scratch_bytes = n_scratch_bytes;
+    }
+    if (root == nullptr) TCX_CUDA_TRY(cudaMalloc(&root, 256));
+    return TCX_OK;
+  }
+  // After an error: nothing of this call may still run when the buffers are next used.
+  void drain() {
+    for (auto& s : slots)
+      if (s.stream) cudaStreamSynchronize(s.stream);
+  }
+};
+
+std::mutex g_contexts_mu;
+std::map<int, std::unique_ptr<FileHashContext>> g_contexts;
+
+FileHashContext* context_for(int device) {
+  std::lock_guard<std::mutex> lock(g_contexts_mu);
+  auto& c = g_contexts[device];
+  if (!c) c = std::make_unique<FileHashContext>();
+  return c.get();
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+tcx_status hash_file_segments(FileHashContext& r, const tcx_file_segment* segs, uint64_t n_segs, uint64_t total,
+                              uint64_t leaf_bytes, uint64_t group_bytes, int depth, int read_threads,
+                              tcx_progress_fn progress, void* progress_ctx, uint8_t root[32]) {
+  const uint64_t n_leaves = (total + leaf_bytes - 1) / leaf_bytes;
+  uint64_t G = std::max<uint64_t>(1, (group_bytes ? group_bytes : kDefaultGroupBytes) / leaf_bytes);
+  G = std::min<uint64_t>(G, n_leaves);
+  const uint64_t gbytes = G * leaf_bytes;
+  const uint64_t n_groups = (n_leaves + G - 1) / G;
+  const int D = static_cast<int>(std::min<uint64_t>(std::max(1, depth > 0 ? depth : kDefaultDepth), n_groups));
+  const int threads = read_threads > 0 ? read_threads
+                                       : std::max(1, std::min(16, static_cast<int>(std::thread::hardware_concurrency())));
+  if (tcx_status st = r.ensure(D, gbytes, n_leaves * 32, std::max<uint64_t>(merkle_scratch_bytes(n_leaves), 256));
+      st != TCX_OK)
+    return st;
+
+  if (progress) progress(0, total, progress_ctx);
+  uint64_t reported = 0;  // groups whose digests are known to be written, reported in order
+  // Reports groups [reported, limit) as their hashes complete; `wait` blocks on each.
+  auto report_done = [&](uint64_t limit, bool wait) -> tcx_status {
+    while (reported < limit) {
+      const Slot& s = r.slots[reported % D];
+      if (s.group != static_cast<int64_t>(reported)) break;  // not enqueued yet
+      const cudaError_t q = wait ? cudaEventSynchronize(s.hashed) : cudaEventQuery(s.hashed);
+      if (q == cudaErrorNotReady) break;
+      if (q != cudaSuccess) return set_error(TCX_INTERNAL, std::string("leaf hashing failed: ") + cudaGetErrorString(q));
+      ++reported;
+      if (progress) progress(std::min(total, reported * gbytes), total, progress_ctx);
+    }
+    return TCX_OK;
+  };
+
+  std::vector<tcx_file_segment> piece;
+  uint64_t seg_i = 0;
+  for (uint64_t k = 0; k < n_groups; ++k) {
+    Slot& s = r.slots[k % D];
+    if (s.group >= 0) {
+      // The slot's previous group (k - depth) is hashed (so also copied out of the
+      // pinned buffer) and reported before the slot's event is recorded again.
+      if (tcx_status st = report_done(k - D + 1, true); st != TCX_OK) return st;
+    }
+    const uint64_t g0 = k * gbytes, g1 = std::min(total, g0 + gbytes);
+    piece.clear();
+    while (seg_i < n_segs && segs[seg_i].dst_offset + segs[seg_i].length <= g0) ++seg_i;
+    for (uint64_t i = seg_i; i < n_segs && segs[i].dst_offset < g1; ++i) {
+      const uint64_t a = std::max(g0, segs[i].dst_offset), b = std::min(g1, segs[i].dst_offset + segs[i].length);
+      if (a >= b) continue;
+      piece.push_back({segs[i].path, segs[i].file_offset + (a - segs[i].dst_offset), a - g0, b - a});
+    }
+    tcx_status st = tcx_read_segments(piece.data(), piece.size(), s.host, threads);
+    if (st == TCX_DATA_LOSS) return set_error(TCX_DATA_LOSS, "short read while hashing source");
+    if (st != TCX_OK) return st;
+    const uint64_t len = g1 - g0;
+    TCX_CUDA_TRY(cudaMemcpyAsync(s.dev, s.host, len, cudaMemcpyHostToDevice, s.stream));
+    const uint64_t first = k * G, n = (len + leaf_bytes - 1) / leaf_bytes;
+    st = launch_leaf_pass(s.dev, len, leaf_bytes, static_cast<uint32_t>(n), 0, ~0ull, nullptr,
+                          r.digests + first * 32, s.stream);
+    if (st != TCX_OK) return st;
+    TCX_CUDA_TRY(cudaEventRecord(s.hashed, s.stream));
+    s.group = static_cast<int64_t>(k);
+    if (tcx_status st2 = report_done(k, false); st2 != TCX_OK) return st2;
+  }
+  // Merkle root on slot 0's stream once every group's digests are written.
+  cudaStream_t fin = r.slots[0].stream;
+  for (int i = 1; i < D; ++i) TCX_CUDA_TRY(cudaStreamWaitEvent(fin, r.slots[i].hashed, 0));
+  if (tcx_status st = launch_merkle(r.digests, n_leaves, r.scratch, r.root, fin); st != TCX_OK) return st;
+  TCX_CUDA_TRY(cudaMemcpyAsync(root, r.root, 32, cudaMemcpyDeviceToHost, fin));
+  TCX_CUDA_TRY(cudaStreamSynchronize(fin));
+  return report_done(n_groups, true);
+}
+
+}  // namespace
+}  // namespace tcx
+
+using namespace tcx;
+
+extern "C" tcx_status tcx_multihash_from_file_segments(const tcx_file_segment* segs, uint64_t n_segs, uint64_t total,
+                                                       uint64_t leaf_bytes, int device, uint64_t group_bytes,
+                                                       int depth, int read_threads, tcx_progress_fn progress,
+                                                       void* progress_ctx, uint8_t* root_out, char* out,
+                                                       uint64_t out_len) {
+  if (total == 0) return set_error(TCX_INVALID_ARGUMENT, "total_size must be > 0");
+  if (leaf_bytes == 0) return set_error(TCX_INVALID_ARGUMENT, "leaf_chunk_bytes must be > 0");
+  if (leaf_bytes > 0xFFFFFFFFull) return set_error(TCX_INVALID_ARGUMENT, "leaf_chunk_bytes must fit in 32 bits");
+  if (out == nullptr || out_len < 57) return set_error(TCX_INVALID_ARGUMENT, "output buffer must hold 57 bytes");
+  if (segs == nullptr && n_segs > 0) return set_error(TCX_INVALID_ARGUMENT, "null segment list");
+  // The segments must tile [0, total) in stream order.
+  uint64_t cursor = 0;
+  for (uint64_t i = 0; i < n_segs; ++i) {
+    if (segs[i].path == nullptr) return set_error(TCX_INVALID_ARGUMENT, "segment without a path");
+    if (segs[i].dst_offset != cursor)
+      return set_errorf(TCX_INVALID_ARGUMENT, "segment %llu starts at %llu, expected %llu",
+                        static_cast<unsigned long long>(i), static_cast<unsigned long long>(segs[i].dst_offset),
+                        static_cast<unsigned long long>(cursor));
+    cursor += segs[i].length;
+  }
+  if (cursor != total)
+    return set_errorf(TCX_INVALID_ARGUMENT, "segments cover %llu bytes, total_size is %llu",
+                      static_cast<unsigned long long>(cursor), static_cast<unsigned long long>(total));
+  int n_dev = 0;
+  TCX_CUDA_TRY(cudaGetDeviceCount(&n_dev));
+  if (device < 0 || device >= n_dev) return set_error(TCX_INVALID_ARGUMENT, "device_id out of range");
+
+  const uint64_t n_leaves = (total + leaf_bytes - 1) / leaf_bytes;
+  if (n_leaves >= (1ull << 32)) return set_error(TCX_INVALID_ARGUMENT, "too many leaves");
+
+  DeviceGuard guard(device);
+  FileHashContext* ctx = context_for(device);
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  uint8_t root[32];
+  const tcx_status st = hash_file_segments(*ctx, segs, n_segs, total, leaf_bytes, group_bytes, depth, read_threads,
+                                           progress, progress_ctx, root);
+  if (st != TCX_OK) {
+    ctx->drain();
+    return st;
+  }
+  if (root_out) std::memcpy(root_out, root, 32);
+  encode_multihash(root, out);
+  return TCX_OK;
+}
+
+extern "C" tcx_status tcx_file_hash_release(int device) {
+  std::lock_guard<std::mutex> lock(g_contexts_mu);
+  for (auto& [dev, ctx] : g_contexts) {
+    if (device >= 0 && dev != device) continue;
+    DeviceGuard guard(dev);
+    std::lock_guard<std::mutex> l(ctx->mu);
+    ctx->free_all();
+  }
+  return TCX_OK;
+}
