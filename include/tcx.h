@@ -271,6 +271,9 @@ typedef struct tcx_load_plan {
   uint64_t window_bytes;         /* bytes per peer per exchange round; bounds the send/receive
                                     scratch to about 2*(N-1) windows (0: 512 MiB) */
   uint64_t flags;                /* TCX_LOAD_* bits */
+  const uint64_t* target_ranges; /* TCX_LOAD_TARGETS: n_targets (offset, length) pairs of this
+                                    rank's view space that are writable; NULL otherwise */
+  uint64_t n_targets;
 } tcx_load_plan;
 
 /* tcx_load_plan.flags: also compute the data multihash of this rank's finished
@@ -286,6 +289,16 @@ typedef struct tcx_load_plan {
  * extraction and transfer are one pass with no pack or receive buffers. NCCL
  * carries only the handle exchange and two one-word barriers. */
 #define TCX_LOAD_PEER_PUSH 2ull
+
+/* tcx_load_plan.flags: the view is a set of separate caller tensors (the
+ * reference's bind_into / mapped-target load, collective_disk_loader.cc:7909-8157,
+ * 5818-6293): d_view is the lowest target's address, view offsets are device
+ * addresses relative to it, and target_ranges lists the writable (offset,
+ * length) ranges. Every job and permute of this rank must lie inside one
+ * target; bytes between targets are never touched (no gap zero-fill). Not
+ * combinable with TCX_LOAD_VIEW_HASH or TCX_LOAD_PEER_PUSH (the exchange uses
+ * NCCL send/recv). */
+#define TCX_LOAD_TARGETS 4ull
 
 /* Per-peer sizes and job lists of the exchange for one rank (host-only planning).
  * Capacities: tcx_plan_exchange_capacity(). pack_jobs move this rank's staged

@@ -74,7 +74,8 @@ class LoadPlan(ctypes.Structure):
     _fields_ = [("total_bytes", _c.c_uint64), ("leaf_bytes", _c.c_uint64), ("stage_bounds", _c.c_void_p),
                 ("jobs", _c.c_void_p), ("job_offsets", _c.c_void_p), ("permutes", _c.c_void_p),
                 ("n_permutes", _c.c_uint64), ("view_bytes", _c.c_uint64), ("slab_bytes", _c.c_uint64),
-                ("window_bytes", _c.c_uint64), ("flags", _c.c_uint64)]
+                ("window_bytes", _c.c_uint64), ("flags", _c.c_uint64), ("target_ranges", _c.c_void_p),
+                ("n_targets", _c.c_uint64)]
 
 
 class ExchangePlan(ctypes.Structure):

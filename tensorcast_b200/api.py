@@ -147,8 +147,7 @@ class Artifact:
     def canonical_index_json(self) -> str:
         return self.index.to_json()
 
-    def tensor_dict(self, *, device, options: GetArtifactOptions | None = None,
-                    ctx: CallContext | None = None) -> dict:
+    def _context(self, device, ctx):
         dev = torch.device(device)
         if dev.type != "cuda":
             raise ArtifactError("this build materialises on CUDA devices only", "UNIMPLEMENTED")
@@ -157,10 +156,15 @@ class Artifact:
         world, rank = (coll.world_size, coll.rank) if coll is not None else (1, 0)
         if world < 1 or not (0 <= rank < world):
             raise ArtifactError("invalid collective group (world_size, rank)", "INVALID_ARGUMENT")
+        return dev, dev_index, coll, world, rank
+
+    def _load(self, dev, dev_index, coll, world, rank, jobs, permutes, view_bytes, d_view=None, alias=False,
+              target_ranges=None) -> dict:
+        """Stages this rank's leaf-aligned range from the files, then one tcx_group_load
+        (hash + exchange + view) into d_view (None: the staged buffer, for an identity view)."""
         T = self.index.total_bytes
         L = self.leaf_chunk_bytes or determine_leaf_chunk_size(T, DEFAULT_LEAF_CHUNK_BYTES)
-        plan = plan_view(self.index, self._spec, self._subset)
-        rank_jobs = gather_rank_jobs(plan.jobs, world)
+        rank_jobs = gather_rank_jobs(jobs, world)
         bounds = stage_bounds(T, L, world)
         lo, hi = bounds[rank], bounds[rank + 1]
         with torch.cuda.device(dev_index):
@@ -169,8 +173,10 @@ class Artifact:
             for off, ln in pad_ranges(self.index, lo, hi):
                 h_stage[off:off + ln].zero_()
             d_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, device=dev)
-            alias = world == 1 and plan.is_identity
-            d_view = d_stage if alias else torch.empty(max(plan.view_bytes, 1), dtype=torch.uint8, device=dev)
+            if alias:
+                d_view = d_stage
+            elif d_view is None:
+                d_view = torch.empty(max(view_bytes, 1), dtype=torch.uint8, device=dev)
             expected = None
             desc = _read_descriptor(self.path) if self.verify_checksums else None
             if desc and desc.get("data_multihash") and not self.leaf_chunk_bytes:
@@ -178,16 +184,86 @@ class Artifact:
             group = _group_for(dev_index, world, rank, coll.group_id if coll else "")
             try:
                 res = group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage,
-                                 permutes=plan.permutes, view_bytes=plan.view_bytes, expected_root=expected)
+                                 permutes=permutes, view_bytes=view_bytes, expected_root=expected,
+                                 target_ranges=target_ranges)
             except _native.TcxError as e:
                 code = {15: "DATA_LOSS", 3: "INVALID_ARGUMENT", 4: "DEADLINE_EXCEEDED"}.get(e.code, "INTERNAL")
                 raise ArtifactError(str(e), code) from e
         self.data_multihash = res["multihash"]
+        res["d_view"] = d_view
+        return res
+
+    def tensor_dict(self, *, device, options: GetArtifactOptions | None = None,
+                    ctx: CallContext | None = None) -> dict:
+        dev, dev_index, coll, world, rank = self._context(device, ctx)
+        plan = plan_view(self.index, self._spec, self._subset)
+        res = self._load(dev, dev_index, coll, world, rank, plan.jobs, plan.permutes, plan.view_bytes,
+                         alias=world == 1 and plan.is_identity)
+        d_view = res["d_view"]
         out = {}
         for t in plan.tensors:
             dt = _TORCH_DTYPES[t.dtype]
             out[t.name] = d_view[t.offset:t.offset + t.nbytes].view(dt).view(t.shape)
         return out
+
+    def bind_into(self, target_tensors, *, mapping=None, packing: str = "byte_space",
+                  options: GetArtifactOptions | None = None, ctx: CallContext | None = None) -> "Binding":
+        """Fills caller-owned CUDA tensors straight from the load (artifact.py:1889-2110).
+
+        Without ``mapping`` the targets are the artifact's (sub)view tensors by name, with
+        the same shapes and dtypes. With ``mapping`` (a copy plan, ``binding.CopyPlanEntry``)
+        each entry copies a checkpoint-tensor slice into a target slice; entries into one
+        target concatenate (mapped_binding.py:287-426 validation). Bytes land in the
+        targets through the load's own copy kernels (TCX_LOAD_TARGETS)."""
+        from . import binding as _b
+        if not isinstance(target_tensors, dict) and not hasattr(target_tensors, "items"):
+            raise ArtifactError("bind_into target_tensors must be a non-empty mapping", "INVALID_ARGUMENT")
+        if not target_tensors:
+            raise ArtifactError("bind_into target_tensors must be a non-empty mapping", "INVALID_ARGUMENT")
+        if str(packing).strip().lower() not in {"append", "plan", "byte_space"}:
+            raise ArtifactError("packing must be 'append', 'plan', or 'byte_space'", "INVALID_ARGUMENT")
+        for name, t in target_tensors.items():
+            if not isinstance(t, torch.Tensor):
+                raise ArtifactError(f"bind_into target '{name}' must be a torch.Tensor", "INVALID_ARGUMENT")
+            if not t.is_cuda:
+                raise ArtifactError(f"bind_into target '{name}' must be CUDA", "FAILED_PRECONDITION")
+        devices = {t.device.index for t in target_tensors.values()}
+        if len(devices) != 1:
+            raise ArtifactError("bind_into targets must share the same CUDA device", "FAILED_PRECONDITION")
+        device = next(iter(target_tensors.values())).device
+        dev, dev_index, coll, world, rank = self._context(device, ctx)
+        base, ranges, view_bytes = _b.target_ranges(target_tensors)
+        if mapping is not None:
+            plan_entries = _b.normalize_copy_plan(mapping)
+            narrows = {}
+            for name, ops in (self._spec.tensors.items() if self._spec else ()):
+                for op in ops:
+                    if hasattr(op, "length"):
+                        narrows[name] = _b.Range(op.dim, op.start, op.start + op.length)
+                    else:
+                        raise ArtifactError("mapping over a transposed view is not supported", "UNIMPLEMENTED")
+            _b.validate_copy_plan(plan=plan_entries, canonical_index=self.index, target_tensors=target_tensors,
+                                  view_narrows=narrows, require_full_coverage=True)
+            jobs = _b.mapped_copy_jobs(plan_entries, self.index, target_tensors, base)
+            permutes = []
+        else:
+            plan = plan_view(self.index, self._spec, self._subset)
+            if set(map(str, target_tensors)) != {t.name for t in plan.tensors}:
+                raise ArtifactError("bind_into target tensors must cover the artifact selection", "FAILED_PRECONDITION")
+            jobs, permutes = _b.view_target_jobs(plan, target_tensors, base)
+        self._load(dev, dev_index, coll, world, rank, jobs, permutes, view_bytes, d_view=base,
+                   target_ranges=ranges)
+        return Binding(dict(target_tensors), self.data_multihash)
+
+
+@dataclass
+class Binding:
+    """The filled targets of a bind_into call and the verified data multihash."""
+    tensors: dict
+    data_multihash: str | None
+
+    def tensor_dict(self) -> dict:
+        return self.tensors
 
 
 def _root_of_multihash(mh: str) -> bytes:

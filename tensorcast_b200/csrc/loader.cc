@@ -240,6 +240,54 @@ tcx_copy_job swap_ends(tcx_copy_job j) {
   return j;
 }
 
+// Every byte this rank's jobs and permutes write lies inside its view and, for a
+// load into separate target tensors, inside one of the targets.
+tcx_status check_destinations(const tcx_load_plan* plan, int rank) {
+  const bool targets = (plan->flags & TCX_LOAD_TARGETS) != 0;
+  std::vector<std::pair<uint64_t, uint64_t>> t;
+  if (targets) {
+    if (plan->flags & (TCX_LOAD_VIEW_HASH | TCX_LOAD_PEER_PUSH))
+      return set_error(TCX_INVALID_ARGUMENT, "a load into target tensors takes neither the view hash nor peer push");
+    if (plan->n_targets == 0 || plan->target_ranges == nullptr)
+      return set_error(TCX_INVALID_ARGUMENT, "TCX_LOAD_TARGETS needs target_ranges");
+    for (uint64_t i = 0; i < plan->n_targets; ++i)
+      t.emplace_back(plan->target_ranges[2 * i], plan->target_ranges[2 * i + 1]);
+    std::sort(t.begin(), t.end());
+    for (size_t i = 0; i < t.size(); ++i) {
+      if (t[i].first + t[i].second > plan->view_bytes || t[i].first + t[i].second < t[i].first)
+        return set_error(TCX_INVALID_ARGUMENT, "a target range exceeds view_bytes");
+      if (i > 0 && t[i].first < t[i - 1].first + t[i - 1].second)
+        return set_error(TCX_INVALID_ARGUMENT, "target ranges overlap");
+    }
+  }
+  auto inside = [&](uint64_t a, uint64_t e) {
+    if (e < a || e > plan->view_bytes) return false;
+    if (!targets) return true;
+    auto it = std::upper_bound(t.begin(), t.end(), std::make_pair(a, ~uint64_t{0}));
+    if (it == t.begin()) return false;
+    --it;
+    return e <= it->first + it->second;
+  };
+  for (uint64_t i = plan->job_offsets[rank]; i < plan->job_offsets[rank + 1]; ++i) {
+    const tcx_copy_job& j = plan->jobs[i];
+    if (j.rows == 0 || j.row_bytes == 0) continue;
+    const uint64_t e = j.dst_off + (j.rows - 1) * (j.rows > 1 ? j.dst_pitch : 0) + j.row_bytes;
+    if (!inside(j.dst_off, e))
+      return set_errorf(TCX_INVALID_ARGUMENT, "job %llu writes outside %s", static_cast<unsigned long long>(i),
+                        targets ? "its target" : "the view");
+  }
+  for (uint64_t i = 0; i < plan->n_permutes; ++i) {
+    const tcx_permute_job& pj = plan->permutes[i];
+    if (pj.ndim == 0 || pj.ndim > TCX_MAX_DIMS) continue;  // rejected by check_permute
+    uint64_t bytes = pj.esize;
+    for (uint32_t d = 0; d < pj.ndim; ++d) bytes *= static_cast<uint64_t>(pj.shape[d] < 0 ? 0 : pj.shape[d]);
+    if (bytes && !inside(pj.dst_off, pj.dst_off + bytes))
+      return set_errorf(TCX_INVALID_ARGUMENT, "permute %llu lies outside %s", static_cast<unsigned long long>(i),
+                        targets ? "one target" : "the view");
+  }
+  return TCX_OK;
+}
+
 float elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
   float ms = 0;
   if (cudaEventElapsedTime(&ms, a, b) != cudaSuccess) return -1.f;
@@ -398,6 +446,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   if (st != TCX_OK) return st;
   if (d_stage == nullptr || d_view == nullptr || out == nullptr)
     return set_error(TCX_INVALID_ARGUMENT, "d_stage, d_view and out are required");
+  if ((st = check_destinations(plan, g->rank)) != TCX_OK) return st;
   TCX_CUDA_TRY(cudaSetDevice(g->device));
   const int world = g->world, rank = g->rank;
   const uint64_t* b = plan->stage_bounds;
@@ -424,7 +473,15 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   // and gap zero-fill waits for the hash passes that read the same bytes.
   const auto* vb = static_cast<const uint8_t*>(d_view);
   const auto* sb = static_cast<const uint8_t*>(d_stage);
-  const bool alias = vb < sb + std::max<uint64_t>(mine, 1) && sb < vb + std::max<uint64_t>(plan->view_bytes, 1);
+  bool alias = vb < sb + std::max<uint64_t>(mine, 1) && sb < vb + std::max<uint64_t>(plan->view_bytes, 1);
+  if (plan->flags & TCX_LOAD_TARGETS) {  // only the targets themselves belong to the view
+    alias = false;
+    for (uint64_t i = 0; i < plan->n_targets; ++i) {
+      const uint8_t* t0 = vb + plan->target_ranges[2 * i];
+      const uint64_t tl = std::max<uint64_t>(plan->target_ranges[2 * i + 1], 1);
+      alias = alias || (t0 < sb + std::max<uint64_t>(mine, 1) && sb < t0 + tl);
+    }
+  }
   std::vector<tcx_copy_job> local_kept;
   for (uint64_t i = 0; i < xp.n_local; ++i) {
     const tcx_copy_job& j = local[i];
@@ -655,8 +712,11 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     TCX_CUDA_TRY(cudaMemcpyAsync(dj, hj, n_jobs_all * sizeof(tcx_copy_job), cudaMemcpyHostToDevice, g->s_comm));
   TCX_CUDA_TRY(cudaEventRecord(g->ev_exch, g->s_comm));  // job tables uploaded, staged bytes complete
   TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->ev_exch, 0));
-  for (uint64_t k = 0; k < xp.n_gaps; ++k)
-    TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
+  // View bytes no job writes are zero-filled, as a fresh view buffer is; bytes
+  // between target tensors belong to no one and are left alone.
+  if ((plan->flags & TCX_LOAD_TARGETS) == 0)
+    for (uint64_t k = 0; k < xp.n_gaps; ++k)
+      TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
   if (!local_kept.empty() &&
       (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), g->s_comm)) != TCX_OK)
     return st;

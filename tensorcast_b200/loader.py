@@ -20,6 +20,7 @@ from .views import JOB_DTYPE, permute_array
 
 VIEW_HASH = 1  # TCX_LOAD_VIEW_HASH
 PEER_PUSH = 2  # TCX_LOAD_PEER_PUSH
+TARGETS = 4  # TCX_LOAD_TARGETS
 
 
 def stage_bounds(total: int, leaf: int, world: int) -> list[int]:
@@ -44,8 +45,9 @@ class _Plan:
     """A tcx_load_plan with its arrays kept alive."""
 
     def __init__(self, total, leaf, bounds, rank_jobs, permutes=(), view_bytes=0, slab_bytes=0, window_bytes=0,
-                 flags=0):
+                 flags=0, target_ranges=None):
         self.bounds = np.ascontiguousarray(bounds, dtype=np.uint64)
+        self.targets = None if target_ranges is None else np.ascontiguousarray(target_ranges, dtype=np.uint64).ravel()
         self.jobs, self.job_offsets = _jobs_concat(rank_jobs)
         self.perms = permute_array(list(permutes)) if permutes else None
         self.c = _native.LoadPlan(
@@ -53,7 +55,9 @@ class _Plan:
             jobs=self.jobs.ctypes.data, job_offsets=self.job_offsets.ctypes.data,
             permutes=self.perms.ctypes.data if self.perms is not None else None,
             n_permutes=0 if self.perms is None else len(self.perms), view_bytes=int(view_bytes),
-            slab_bytes=int(slab_bytes), window_bytes=int(window_bytes), flags=int(flags))
+            slab_bytes=int(slab_bytes), window_bytes=int(window_bytes), flags=int(flags),
+            target_ranges=None if self.targets is None else self.targets.ctypes.data,
+            n_targets=0 if self.targets is None else len(self.targets) // 2)
 
 
 def plan_exchange(total, leaf, bounds, rank_jobs, rank, view_bytes=0) -> dict:
@@ -159,14 +163,18 @@ class Group:
 
     def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, permutes=(), view_bytes=None,
              expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0,
-             view_hash: bool = False, peer_push: bool = False) -> dict:
-        """peer_push: exchange by writing into the peers' views over NVLink (d_view must be a
-        cudaMalloc allocation of this process, e.g. a torch CUDA tensor); else NCCL send/recv."""
-        """Runs one load; returns the result fields as a dict. h_stage None: device-resident."""
+             view_hash: bool = False, peer_push: bool = False, target_ranges=None) -> dict:
+        """Runs one load; returns the result fields as a dict. h_stage None: device-resident.
+
+        peer_push: exchange by writing into the peers' views over NVLink (d_view must be a
+        cudaMalloc allocation of this process, e.g. a torch CUDA tensor); else NCCL send/recv.
+        target_ranges: (offset, length) pairs of separate target tensors (TCX_LOAD_TARGETS):
+        d_view is then the lowest target's address and view offsets are relative to it."""
         if view_bytes is None:
             view_bytes = d_view.numel() * d_view.element_size() if isinstance(d_view, torch.Tensor) else 0
         plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes, window_bytes,
-                     flags=(VIEW_HASH if view_hash else 0) | (PEER_PUSH if peer_push else 0))
+                     flags=(VIEW_HASH if view_hash else 0) | (PEER_PUSH if peer_push else 0) |
+                     (TARGETS if target_ranges is not None else 0), target_ranges=target_ranges)
         res = _native.LoadResult()
         exp = None
         if expected_root is not None:

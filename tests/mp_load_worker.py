@@ -77,6 +77,36 @@ def main() -> int:
                 if res["root"] != want_root or got.size != want.size or not (got == want).all():
                     print(f"rank {rank}: case {name} host={host} window={window} push={push} FAILED", flush=True)
                     failures += 1
+        # Separate target tensors (bind_into, TCX_LOAD_TARGETS) over the NCCL exchange:
+        # the Llama TP views with every tensor in its own allocation, guard bytes around.
+        from tensorcast_b200.binding import target_ranges, view_target_jobs
+        canon, meta = oviews.canonical_bytes(llama)
+        index = index_from_meta(meta, canon.size)
+        sl = oviews.tp_slices(meta, world, rank)
+        plan = plan_view(index, ViewSpec({n: [NarrowOp(*v)] for n, v in sl.items()}))
+        guards, targets = [], {}
+        for t in reversed(plan.tensors):
+            g = torch.full((t.nbytes + 512,), 0xA5, dtype=torch.uint8, device="cuda")
+            guards.append(g)
+            targets[t.name] = g[256:256 + t.nbytes]
+        base, ranges, vbytes = target_ranges(targets)
+        jobs, _ = view_target_jobs(plan, targets, base)
+        leaf = 1 << 16
+        bounds = stage_bounds(canon.size, leaf, world)
+        lo, hi = bounds[rank], bounds[rank + 1]
+        h = torch.empty(max(hi - lo, 1), dtype=torch.uint8, pin_memory=True)
+        h.numpy()[: hi - lo] = canon[lo:hi]
+        d_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, device="cuda")
+        want_root = oracle.tree_root(oracle.leaf_digests(canon, leaf))
+        res = group.load(canon.size, leaf, bounds, gather_rank_jobs(jobs, world), d_stage=d_stage, d_view=base,
+                         h_stage=h, view_bytes=vbytes, expected_root=want_root, slab_bytes=256, window_bytes=4096,
+                         target_ranges=ranges)
+        want = oviews.materialize_view(canon, meta, sl, {}, None)
+        same = all((targets[t.name].cpu().numpy() == want[t.offset:t.offset + t.nbytes]).all() for t in plan.tensors)
+        guard_ok = all(bool((g[:256] == 0xA5).all()) and bool((g[-256:] == 0xA5).all()) for g in guards)
+        if res["root"] != want_root or want.size != plan.view_bytes or not same or not guard_ok:
+            print(f"rank {rank}: bind-into targets case FAILED", flush=True)
+            failures += 1
         ok = torch.tensor([failures], device="cuda")
         dist.all_reduce(ok)
         failures = int(ok.item())
