@@ -332,8 +332,22 @@ uint64_t tcx_plan_exchange_capacity(const tcx_load_plan* plan, int world);
 tcx_status tcx_plan_exchange(const tcx_load_plan* plan, int world, int rank, tcx_exchange_plan* out);
 
 /* Reads segments into dst (pinned or pageable host memory) with `threads`
- * parallel preads; a short read is DATA_LOSS (source_hash.cc:44-51). */
+ * parallel preads; a short read is DATA_LOSS (source_hash.cc:44-51).
+ * Equivalent to tcx_read_segments_ex(segs, n, dst, threads, 0). */
 tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n, void* dst, int threads);
+
+/* tcx_read_segments_ex flag: bypass the page cache (O_DIRECT) for cold reads;
+ * files on a file system that refuses O_DIRECT are read buffered. */
+#define TCX_READ_DIRECT 1ull
+
+/* tcx_read_segments with flags. Pieces are read in source order (file, then
+ * offset), each thread reading forward, whatever order the segments are listed
+ * in: the source-ordered windows of the reference's safetensors readers
+ * (PreadMultiSafetensorsSource / DirectAlignedSafetensorsSource,
+ * collective_disk_loader.cc:1571-2200). With TCX_READ_DIRECT, nearby pieces
+ * (gaps up to 256 KiB) are read as one 4 KiB-aligned window of at most 16 MiB
+ * into an aligned bounce buffer and copied out, so segments need no alignment. */
+tcx_status tcx_read_segments_ex(const tcx_file_segment* segs, uint64_t n, void* dst, int threads, uint64_t flags);
 
 /* Progress of a streamed hash: bytes whose leaves are hashed so far, of total. */
 typedef void (*tcx_progress_fn)(uint64_t processed_bytes, uint64_t total_bytes, void* ctx);
@@ -346,7 +360,8 @@ typedef void (*tcx_progress_fn)(uint64_t processed_bytes, uint64_t total_bytes, 
  * = stream offset; they must tile [0, total) exactly), cut into leaves of
  * leaf_bytes (used as given, no adaptive policy, as the CPU path), SHA-256 per
  * leaf, Merkle tree, multihash. Groups of whole leaves (group_bytes, 0 = 1 GiB)
- * are read by read_threads parallel preads (0 = up to 16) into `depth` pinned
+ * are read by read_threads parallel preads (0 = up to 16; read_flags as
+ * tcx_read_segments_ex, e.g. TCX_READ_DIRECT) into `depth` pinned
  * slots (0 = 4), copied to the device and hashed on one stream per slot, so
  * reads, copies and hashing overlap. The slots stay allocated per device for
  * the next call (tcx_file_hash_release frees them); calls on one device are
@@ -357,8 +372,8 @@ typedef void (*tcx_progress_fn)(uint64_t processed_bytes, uint64_t total_bytes, 
  * multihash. progress (optional) is called on the calling thread. */
 tcx_status tcx_multihash_from_file_segments(const tcx_file_segment* segs, uint64_t n_segs, uint64_t total,
                                             uint64_t leaf_bytes, int device, uint64_t group_bytes, int depth,
-                                            int read_threads, tcx_progress_fn progress, void* progress_ctx,
-                                            uint8_t* root_out, char* out, uint64_t out_len);
+                                            int read_threads, uint64_t read_flags, tcx_progress_fn progress,
+                                            void* progress_ctx, uint8_t* root_out, char* out, uint64_t out_len);
 
 /* Frees the pinned and device buffers tcx_multihash_from_file_segments keeps for
  * `device` (-1: every device). No counterpart in the reference (it allocates per

@@ -69,6 +69,7 @@ class CallContext:
 @dataclass(frozen=True)
 class GetArtifactOptions:
     export_policy: str | None = None
+    direct_io: bool = False  # stage with O_DIRECT reads (cold block devices); buffered where refused
 
 
 _GROUPS: dict = {}
@@ -159,7 +160,7 @@ class Artifact:
         return dev, dev_index, coll, world, rank
 
     def _load(self, dev, dev_index, coll, world, rank, jobs, permutes, view_bytes, d_view=None, alias=False,
-              target_ranges=None) -> dict:
+              target_ranges=None, options: GetArtifactOptions | None = None) -> dict:
         """Stages this rank's leaf-aligned range from the files, then one tcx_group_load
         (hash + exchange + view) into d_view (None: the staged buffer, for an identity view)."""
         T = self.index.total_bytes
@@ -169,7 +170,8 @@ class Artifact:
         lo, hi = bounds[rank], bounds[rank + 1]
         with torch.cuda.device(dev_index):
             h_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, pin_memory=True)
-            read_segments(canonical_segments(self.index, lo, hi), h_stage.data_ptr(), threads=min(16, os.cpu_count() or 4))
+            read_segments(canonical_segments(self.index, lo, hi), h_stage.data_ptr(), threads=min(16, os.cpu_count() or 4),
+                          direct=bool(options and options.direct_io))
             for off, ln in pad_ranges(self.index, lo, hi):
                 h_stage[off:off + ln].zero_()
             d_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, device=dev)
@@ -198,7 +200,7 @@ class Artifact:
         dev, dev_index, coll, world, rank = self._context(device, ctx)
         plan = plan_view(self.index, self._spec, self._subset)
         res = self._load(dev, dev_index, coll, world, rank, plan.jobs, plan.permutes, plan.view_bytes,
-                         alias=world == 1 and plan.is_identity)
+                         alias=world == 1 and plan.is_identity, options=options)
         d_view = res["d_view"]
         out = {}
         for t in plan.tensors:
@@ -252,7 +254,7 @@ class Artifact:
                 raise ArtifactError("bind_into target tensors must cover the artifact selection", "FAILED_PRECONDITION")
             jobs, permutes = _b.view_target_jobs(plan, target_tensors, base)
         self._load(dev, dev_index, coll, world, rank, jobs, permutes, view_bytes, d_view=base,
-                   target_ranges=ranges)
+                   target_ranges=ranges, options=options)
         return Binding(dict(target_tensors), self.data_multihash)
 
 

@@ -139,7 +139,7 @@ struct DeviceGuard {
 
 tcx_status hash_file_segments(FileHashContext& r, const tcx_file_segment* segs, uint64_t n_segs, uint64_t total,
                               uint64_t leaf_bytes, uint64_t group_bytes, int depth, int read_threads,
-                              tcx_progress_fn progress, void* progress_ctx, uint8_t root[32]) {
+                              uint64_t read_flags, tcx_progress_fn progress, void* progress_ctx, uint8_t root[32]) {
   const uint64_t n_leaves = (total + leaf_bytes - 1) / leaf_bytes;
   uint64_t G = std::max<uint64_t>(1, (group_bytes ? group_bytes : kDefaultGroupBytes) / leaf_bytes);
   G = std::min<uint64_t>(G, n_leaves);
@@ -185,7 +185,7 @@ tcx_status hash_file_segments(FileHashContext& r, const tcx_file_segment* segs, 
       if (a >= b) continue;
       piece.push_back({segs[i].path, segs[i].file_offset + (a - segs[i].dst_offset), a - g0, b - a});
     }
-    tcx_status st = tcx_read_segments(piece.data(), piece.size(), s.host, threads);
+    tcx_status st = tcx_read_segments_ex(piece.data(), piece.size(), s.host, threads, read_flags);
     if (st == TCX_DATA_LOSS) return set_error(TCX_DATA_LOSS, "short read while hashing source");
     if (st != TCX_OK) return st;
     const uint64_t len = g1 - g0;
@@ -214,7 +214,8 @@ using namespace tcx;
 
 extern "C" tcx_status tcx_multihash_from_file_segments(const tcx_file_segment* segs, uint64_t n_segs, uint64_t total,
                                                        uint64_t leaf_bytes, int device, uint64_t group_bytes,
-                                                       int depth, int read_threads, tcx_progress_fn progress,
+                                                       int depth, int read_threads, uint64_t read_flags,
+                                                       tcx_progress_fn progress,
                                                        void* progress_ctx, uint8_t* root_out, char* out,
                                                        uint64_t out_len) {
   if (total == 0) return set_error(TCX_INVALID_ARGUMENT, "total_size must be > 0");
@@ -247,7 +248,7 @@ extern "C" tcx_status tcx_multihash_from_file_segments(const tcx_file_segment* s
   std::lock_guard<std::mutex> lock(ctx->mu);
   uint8_t root[32];
   const tcx_status st = hash_file_segments(*ctx, segs, n_segs, total, leaf_bytes, group_bytes, depth, read_threads,
-                                           progress, progress_ctx, root);
+                                           read_flags, progress, progress_ctx, root);
   if (st != TCX_OK) {
     ctx->drain();
     return st;

@@ -47,6 +47,13 @@ using Clock = std::chrono::steady_clock;
 constexpr uint64_t kDefaultSlab = 256 * 1024;
 constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchange round
 
+// Copy kernels of a load run while the leaf hash is still going, and the hash's
+// consumer warps are bound by their own instruction issue: a full 8-CTA-per-SM
+// copy grid shares every SMSP with them and slows the chains (measured: the
+// 70B TP-4 hash went from about 80 to 135 ms). A quarter of the SMs' worth of
+// CTAs still moves several hundred GB/s over NVLink or HBM.
+uint32_t load_copy_ctas() { return static_cast<uint32_t>(std::max(8, sm_count() / 4)); }
+
 std::string nccl_msg(ncclResult_t r) { return std::string(ncclGetErrorString(r)); }
 
 struct DevBuf {
@@ -379,63 +386,6 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   return TCX_OK;
 }
 
-extern "C" tcx_status tcx_read_segments(const tcx_file_segment* segs, uint64_t n, void* dst, int threads) {
-  if (n == 0) return TCX_OK;
-  if (segs == nullptr || dst == nullptr) return set_error(TCX_INVALID_ARGUMENT, "null pointer");
-  // Split every segment into <= 64 MiB pieces and spread them over the threads.
-  struct Piece {
-    const char* path;
-    uint64_t file_off, dst_off, len;
-  };
-  std::vector<Piece> pieces;
-  constexpr uint64_t kPiece = 64ull << 20;
-  for (uint64_t i = 0; i < n; ++i)
-    for (uint64_t o = 0; o < segs[i].length; o += kPiece)
-      pieces.push_back({segs[i].path, segs[i].file_offset + o, segs[i].dst_offset + o,
-                        std::min(kPiece, segs[i].length - o)});
-  const int nt = std::max(1, std::min<int>(threads, static_cast<int>(pieces.size())));
-  std::atomic<uint64_t> next{0};
-  std::atomic<int> status{TCX_OK};
-  std::vector<std::string> errors(nt);
-  auto worker = [&](int t) {
-    std::string open_path;
-    int fd = -1;
-    for (uint64_t k = next++; k < pieces.size() && status.load() == TCX_OK; k = next++) {
-      const Piece& p = pieces[k];
-      if (fd < 0 || open_path != p.path) {
-        if (fd >= 0) close(fd);
-        fd = open(p.path, O_RDONLY | O_CLOEXEC);
-        open_path = p.path;
-        if (fd < 0) {
-          errors[t] = std::string("open failed: ") + p.path;
-          status = TCX_NOT_FOUND;
-          break;
-        }
-      }
-      uint64_t got = 0;
-      while (got < p.len) {
-        const ssize_t r = pread(fd, static_cast<uint8_t*>(dst) + p.dst_off + got, p.len - got, p.file_off + got);
-        if (r <= 0) {
-          errors[t] = std::string("short read while loading source: ") + p.path;
-          status = TCX_DATA_LOSS;
-          break;
-        }
-        got += static_cast<uint64_t>(r);
-      }
-    }
-    if (fd >= 0) close(fd);
-  };
-  std::vector<std::thread> pool;
-  for (int t = 1; t < nt; ++t) pool.emplace_back(worker, t);
-  worker(0);
-  for (auto& th : pool) th.join();
-  if (status != TCX_OK) {
-    for (const auto& e : errors)
-      if (!e.empty()) return set_error(status, e);
-  }
-  return status;
-}
-
 extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage,
                                      void* d_view, const uint8_t* expected_root, tcx_load_result* out,
                                      void* stream) {
@@ -718,7 +668,8 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     for (uint64_t k = 0; k < xp.n_gaps; ++k)
       TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
   if (!local_kept.empty() &&
-      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), g->s_comm)) != TCX_OK)
+      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), g->s_comm,
+                            false, load_copy_ctas())) != TCX_OK)
     return st;
   uint64_t sent = 0, received = 0;
   if (push) {
@@ -728,7 +679,8 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
       const uint64_t n = push_off[p + 1] - push_off[p];
       if (p == rank || n == 0) continue;
       uint8_t* peer_view = static_cast<uint8_t*>(g->peer_views[p].base) + g->peer_views[p].offset;
-      if ((st = launch_copy_jobs(stage, peer_view, dj + o_push + push_off[p], n, prefix_for(n), g->s_comm, true)) != TCX_OK)
+      if ((st = launch_copy_jobs(stage, peer_view, dj + o_push + push_off[p], n, prefix_for(n), g->s_comm, true,
+                                 load_copy_ctas())) != TCX_OK)
         return st;
     }
     // Every peer has finished writing into this rank's view.
@@ -743,7 +695,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     if (k >= 2) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->sent_events[k - 2], 0));
     const uint64_t np = pack_off[k + 1] - pack_off[k];
     if (np && (st = launch_copy_jobs(stage, g->send.p, dj + o_pack + pack_off[k], np,
-                                     prefix_for(np), g->s_pack)) != TCX_OK)
+                                     prefix_for(np), g->s_pack, false, load_copy_ctas())) != TCX_OK)
       return st;
     TCX_CUDA_TRY(cudaEventRecord(g->packed_events[k], g->s_pack));
     TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[k], 0));
@@ -770,7 +722,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
     const uint64_t ns = scat_off[k + 1] - scat_off[k];
     if (ns && (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter + scat_off[k], ns,
-                                     prefix_for(ns), g->s_comm)) != TCX_OK)
+                                     prefix_for(ns), g->s_comm, false, load_copy_ctas())) != TCX_OK)
       return st;
   }
   for (uint64_t i = 0; i < plan->n_permutes; ++i) {

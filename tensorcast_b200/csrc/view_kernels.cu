@@ -307,16 +307,6 @@ __global__ void permute_generic_kernel(const T* __restrict__ src, T* __restrict_
   }
 }
 
-int sm_count() {
-  static thread_local int dev_cached = -1, sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess && dev != dev_cached) {
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    dev_cached = dev;
-  }
-  return sms;
-}
-
 template <typename T>
 tcx_status launch_permute_t(const uint8_t* src, uint8_t* dst, const tcx_permute_job& pj, cudaStream_t stream) {
   uint64_t numel = 1;
@@ -363,13 +353,25 @@ tcx_status launch_permute_t(const uint8_t* src, uint8_t* dst, const tcx_permute_
 
 }  // namespace
 
+// SM count of the current device (cached per thread).
+int sm_count() {
+  static thread_local int dev_cached = -1, sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev != dev_cached) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    dev_cached = dev;
+  }
+  return sms;
+}
+
 tcx_status launch_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* d_jobs, uint64_t n_jobs,
-                            uint64_t* d_prefix, cudaStream_t stream, bool remote_dst) {
+                            uint64_t* d_prefix, cudaStream_t stream, bool remote_dst, uint32_t max_ctas) {
   if (n_jobs == 0) return TCX_OK;
   copy_prefix_kernel<<<1, 1024, 0, stream>>>(d_jobs, n_jobs, d_prefix);
   note_launches(1);
   TCX_CUDA_TRY(cudaGetLastError());
-  const unsigned grid = static_cast<unsigned>(sm_count()) * 8u;
+  unsigned grid = static_cast<unsigned>(sm_count()) * 8u;
+  if (max_ctas) grid = std::min<unsigned>(grid, max_ctas);
   copy_jobs_kernel<<<grid, kCopyThreads, 0, stream>>>(static_cast<const uint8_t*>(d_src),
                                                       static_cast<uint8_t*>(d_dst), d_jobs, n_jobs, d_prefix, remote_dst);
   note_launches(1);

@@ -139,8 +139,10 @@ def disk_dir_layout(artifact_dir) -> tuple[list[tuple[str, int, int, int]], int,
 
 def compute_data_multihash_from_segments(segments, total: int, *, device_id: int = 0,
                                          leaf_chunk_bytes: int = HASH_LEAF_CHUNK_BYTES, progress_cb=None,
-                                         group_bytes: int = 0, depth: int = 0, read_threads: int = 0) -> str:
-    """Multihash of the byte stream given as (path, file_offset, stream_offset, length) segments."""
+                                         group_bytes: int = 0, depth: int = 0, read_threads: int = 0,
+                                         direct_io: bool = False) -> str:
+    """Multihash of the byte stream given as (path, file_offset, stream_offset, length) segments;
+    direct_io reads past the page cache (O_DIRECT windows, buffered where refused)."""
     arr = (_native.FileSegment * max(len(segments), 1))()
     keep = []
     for i, (path, foff, soff, ln) in enumerate(segments):
@@ -154,7 +156,7 @@ def compute_data_multihash_from_segments(segments, total: int, *, device_id: int
     out = ctypes.create_string_buffer(64)
     try:
         _native.call("tcx_multihash_from_file_segments", arr, len(segments), int(total), int(leaf_chunk_bytes),
-                     int(device_id), int(group_bytes), int(depth), int(read_threads),
+                     int(device_id), int(group_bytes), int(depth), int(read_threads), 1 if direct_io else 0,
                      ctypes.cast(cb, ctypes.c_void_p) if cb is not None else None, None, root, out, 64)
     except _native.TcxError as e:
         code = {3: "INVALID_ARGUMENT", 5: "NOT_FOUND", 12: "UNIMPLEMENTED", 15: "DATA_LOSS"}.get(e.code, "INTERNAL")
@@ -163,14 +165,16 @@ def compute_data_multihash_from_segments(segments, total: int, *, device_id: int
 
 
 def compute_data_multihash_from_disk_dir(artifact_dir, progress_cb=None, *, device_id: int = 0,
-                                         group_bytes: int = 0, depth: int = 0, read_threads: int = 0) -> str:
+                                         group_bytes: int = 0, depth: int = 0, read_threads: int = 0,
+                                         direct_io: bool = False) -> str:
     """compute_data_multihash_from_disk_dir (disk_dir_hash.cc:47-104), hashed on the GPU.
 
     progress_cb(processed_bytes, total_bytes) is called with (0, total) first and then as
     groups of leaves finish, as the reference's leaf progress adapter does (:29-45)."""
     segs, total, _ = disk_dir_layout(artifact_dir)
     return compute_data_multihash_from_segments(segs, total, device_id=device_id, progress_cb=progress_cb,
-                                                group_bytes=group_bytes, depth=depth, read_threads=read_threads)
+                                                group_bytes=group_bytes, depth=depth, read_threads=read_threads,
+                                                direct_io=direct_io)
 
 
 def release_buffers(device_id: int = -1) -> None:

@@ -84,8 +84,12 @@ def plan_exchange(total, leaf, bounds, rank_jobs, rank, view_bytes=0) -> dict:
     return out
 
 
-def read_segments(segments, dst_ptr: int, threads: int = 8) -> None:
-    """Parallel preads of (path, file_offset, dst_offset, length) segments into dst_ptr."""
+READ_DIRECT = 1  # TCX_READ_DIRECT
+
+
+def read_segments(segments, dst_ptr: int, threads: int = 8, direct: bool = False) -> None:
+    """Parallel preads of (path, file_offset, dst_offset, length) segments into dst_ptr, in
+    source order; direct: O_DIRECT through aligned windows (cold reads past the page cache)."""
     if not segments:
         return
     arr = (_native.FileSegment * len(segments))()
@@ -94,7 +98,7 @@ def read_segments(segments, dst_ptr: int, threads: int = 8) -> None:
         p = os.fsencode(path)
         keep.append(p)
         arr[i] = _native.FileSegment(p, foff, doff, ln)
-    _native.call("tcx_read_segments", arr, len(segments), dst_ptr, int(threads))
+    _native.call("tcx_read_segments_ex", arr, len(segments), dst_ptr, int(threads), READ_DIRECT if direct else 0)
 
 
 def bind_device_cpus(device: int) -> int:
