@@ -79,6 +79,7 @@ def main() -> int:
                     failures += 1
         # Separate target tensors (bind_into, TCX_LOAD_TARGETS) over the NCCL exchange:
         # the Llama TP views with every tensor in its own allocation, guard bytes around.
+        from tensorcast_b200.api import _TORCH_DTYPES
         from tensorcast_b200.binding import target_ranges, view_target_jobs
         canon, meta = oviews.canonical_bytes(llama)
         index = index_from_meta(meta, canon.size)
@@ -88,7 +89,7 @@ def main() -> int:
         for t in reversed(plan.tensors):
             g = torch.full((t.nbytes + 512,), 0xA5, dtype=torch.uint8, device="cuda")
             guards.append(g)
-            targets[t.name] = g[256:256 + t.nbytes]
+            targets[t.name] = g[256:256 + t.nbytes].view(_TORCH_DTYPES[t.dtype]).view(t.shape)
         base, ranges, vbytes = target_ranges(targets)
         jobs, _ = view_target_jobs(plan, targets, base)
         leaf = 1 << 16
@@ -102,7 +103,8 @@ def main() -> int:
                          h_stage=h, view_bytes=vbytes, expected_root=want_root, slab_bytes=256, window_bytes=4096,
                          target_ranges=ranges)
         want = oviews.materialize_view(canon, meta, sl, {}, None)
-        same = all((targets[t.name].cpu().numpy() == want[t.offset:t.offset + t.nbytes]).all() for t in plan.tensors)
+        same = all((targets[t.name].reshape(-1).view(torch.uint8).cpu().numpy() == want[t.offset:t.offset + t.nbytes]).all()
+                   for t in plan.tensors)
         guard_ok = all(bool((g[:256] == 0xA5).all()) and bool((g[-256:] == 0xA5).all()) for g in guards)
         if res["root"] != want_root or want.size != plan.view_bytes or not same or not guard_ok:
             print(f"rank {rank}: bind-into targets case FAILED", flush=True)
