@@ -52,7 +52,7 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", choices=["push", "nccl"], default="push",
-                    help="N>1 shard exchange: push over peer memory (copy kernels writing into the peers' views "
+                    help="N>1 shard exchange: push over peer memory (copy-engine copies into the peers' views "
                          "over NVLink) or NCCL send/recv of packed windows")
     ap.add_argument("--stage", choices=["mapped", "pinned"], default="pinned",
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
@@ -576,7 +576,7 @@ def main() -> None:
                              + (f"; {transposed} stored [in, out] and read whole through a transpose view"
                                 if transposed else "")),
                 "artifact_bytes": T, "leaf_bytes": L, "leaves": first["leaves"],
-                "exchange": ("push over peer memory (NVLink P2P stores from the copy kernels)"
+                "exchange": ("push over peer memory (copy-engine 2-D copies into the peers' views over NVLink)"
                              if args.exchange == "push" else "NCCL send/recv of packed windows") if world > 1 else "none",
                 "view_bytes_per_rank": mine.view_bytes, "parallelism": f"tp{world}",
                 "l2": "inputs (staged bytes) far larger than the 126 MB L2; no flush needed",

@@ -284,10 +284,12 @@ typedef struct tcx_load_plan {
 
 /* tcx_load_plan.flags: exchange by pushing over peer memory instead of NCCL
  * send/recv: every rank maps every peer's view (CUDA IPC; d_view must be memory
- * this process allocated with cudaMalloc) and its copy kernels write the peers'
- * view pieces from its staged bytes directly into those views over NVLink, so
- * extraction and transfer are one pass with no pack or receive buffers. NCCL
- * carries only the handle exchange and two one-word barriers. */
+ * this process allocated with cudaMalloc) and copies the peers' view pieces
+ * from its staged bytes directly into those views over NVLink with the copy
+ * engines (one 2-D copy per piece, one stream per peer), so extraction and
+ * transfer are one pass with no pack or receive buffers and no SM time is taken
+ * from the leaf hash running at the same time. NCCL carries only the handle
+ * exchange and two one-word barriers. */
 #define TCX_LOAD_PEER_PUSH 2ull
 
 /* tcx_load_plan.flags: the view is a set of separate caller tensors (the

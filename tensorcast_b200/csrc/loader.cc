@@ -47,12 +47,17 @@ using Clock = std::chrono::steady_clock;
 constexpr uint64_t kDefaultSlab = 256 * 1024;
 constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchange round
 
-// Copy kernels of a load run while the leaf hash is still going, and the hash's
-// consumer warps are bound by their own instruction issue: a full 8-CTA-per-SM
-// copy grid shares every SMSP with them and slows the chains (measured: the
-// 70B TP-4 hash went from about 80 to 135 ms). A quarter of the SMs' worth of
-// CTAs still moves several hundred GB/s over NVLink or HBM.
-uint32_t load_copy_ctas() { return static_cast<uint32_t>(std::max(8, sm_count() / 4)); }
+// Copy kernels of a load run while the leaf hash is still going. With fewer
+// chains than about one consumer warp per SMSP the hash is bound by each
+// warp's own instruction issue, and a full 8-CTA-per-SM copy grid sharing those
+// SMSPs slows every chain (measured: the 70B TP-4 hash went from about 80 to
+// 135 ms); a quarter of the SMs' worth of CTAs still moves several hundred GB/s
+// over NVLink or HBM. With more chains than that the hash is throughput-bound
+// like the copies, and the copies keep the full grid.
+uint32_t load_copy_ctas(uint64_t n_chains) {
+  const uint64_t sms = static_cast<uint64_t>(sm_count());
+  return n_chains < sms * 128 ? static_cast<uint32_t>(std::max<uint64_t>(8, sms / 4)) : 0u;
+}
 
 std::string nccl_msg(ncclResult_t r) { return std::string(ncclGetErrorString(r)); }
 
@@ -103,6 +108,11 @@ struct tcx_group {
     bool open = false;
   };
   std::vector<PeerView> peer_views;
+  // One stream per peer for the push copies (copy engines), so the pushes to
+  // different peers run at once on different engines.
+  std::vector<cudaStream_t> s_peer;
+  std::vector<cudaEvent_t> peer_done;
+  cudaEvent_t ev_push = nullptr;
   DevBuf ipc_records, barrier_word;
   uint8_t* h_ipc = nullptr;  // pinned, world records
 };
@@ -368,9 +378,16 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   for (DevBuf* b : {&g->digests_mine, &g->states, &g->digests_all, &g->digests_compact, &g->merkle_scratch, &g->root,
                     &g->send, &g->recv, &g->perm_scratch, &g->jobs, &g->prefix, &g->view_digests, &g->view_scratch})
     b->release();
-  g->peer_views.clear();
+  for (cudaStream_t s : g->s_peer)
+    if (s) cudaStreamSynchronize(s);
   for (auto& pv : g->peer_views)
     if (pv.open) cudaIpcCloseMemHandle(pv.base);
+  g->peer_views.clear();
+  for (cudaEvent_t e : g->peer_done)
+    if (e) cudaEventDestroy(e);
+  if (g->ev_push) cudaEventDestroy(g->ev_push);
+  for (cudaStream_t s : g->s_peer)
+    if (s) cudaStreamDestroy(s);
   g->ipc_records.release();
   g->barrier_word.release();
   if (g->h_ipc) cudaFreeHost(g->h_ipc);
@@ -514,7 +531,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     scat_off[k + 1] = round_scatter.size();
   }
 
-  // Push exchange: this rank writes each peer's view pieces from its staged range
+  // Push exchange: this rank copies each peer's view pieces from its staged range
   // straight into the peer's view over NVLink (no pack or receive buffers).
   const bool push = world > 1 && (plan->flags & TCX_LOAD_PEER_PUSH) != 0;
   std::vector<tcx_copy_job> push_jobs;
@@ -541,9 +558,8 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   }
 
   // --- buffers --------------------------------------------------------------
-  const uint64_t n_jobs_all =
-      round_pack.size() + local_kept.size() + round_scatter.size() + compact.size() + push_jobs.size();
-  const uint64_t n_launches = 2 * rounds + 2 + static_cast<uint64_t>(world);
+  const uint64_t n_jobs_all = round_pack.size() + local_kept.size() + round_scatter.size() + compact.size();
+  const uint64_t n_launches = 2 * rounds + 2;
   if ((st = g->digests_mine.grow(std::max<uint64_t>(max_n, 1) * 32)) != TCX_OK) return st;
   if ((st = g->states.grow(std::max<uint64_t>(n_mine, 1) * 32)) != TCX_OK) return st;
   if ((st = g->merkle_scratch.grow(merkle_scratch_bytes(n_total))) != TCX_OK) return st;
@@ -577,12 +593,11 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   }
   tcx_copy_job* hj = g->h_jobs;
   const uint64_t o_pack = 0, o_local = round_pack.size(), o_scatter = o_local + local_kept.size(),
-                 o_compact = o_scatter + round_scatter.size(), o_push = o_compact + compact.size();
+                 o_compact = o_scatter + round_scatter.size();
   std::copy(round_pack.begin(), round_pack.end(), hj + o_pack);
   std::copy(local_kept.begin(), local_kept.end(), hj + o_local);
   std::copy(round_scatter.begin(), round_scatter.end(), hj + o_scatter);
   std::copy(compact.begin(), compact.end(), hj + o_compact);
-  std::copy(push_jobs.begin(), push_jobs.end(), hj + o_push);
   auto* dj = static_cast<tcx_copy_job*>(g->jobs.p);
   auto* dprefix = static_cast<uint64_t*>(g->prefix.p);
   // Each copy-job launch gets its own prefix region, handed out in launch order
@@ -601,6 +616,16 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   if (push) {
     // Map every peer's view (collective) and check that each push stays inside it.
     if ((st = map_peer_views(g, d_view, plan->view_bytes, deadline)) != TCX_OK) return st;
+    if (g->s_peer.empty()) {
+      g->s_peer.assign(world, nullptr);
+      g->peer_done.assign(world, nullptr);
+      for (int p = 0; p < world; ++p) {
+        if (p == rank) continue;
+        TCX_CUDA_TRY(cudaStreamCreateWithFlags(&g->s_peer[p], cudaStreamNonBlocking));
+        TCX_CUDA_TRY(cudaEventCreateWithFlags(&g->peer_done[p], cudaEventDisableTiming));
+      }
+      TCX_CUDA_TRY(cudaEventCreateWithFlags(&g->ev_push, cudaEventDisableTiming));
+    }
     for (int p = 0; p < world; ++p) {
       if (p == rank) continue;
       for (uint64_t i = push_off[p]; i < push_off[p + 1]; ++i) {
@@ -669,19 +694,33 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
       TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
   if (!local_kept.empty() &&
       (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), g->s_comm,
-                            false, load_copy_ctas())) != TCX_OK)
+                            load_copy_ctas(n_mine))) != TCX_OK)
     return st;
   uint64_t sent = 0, received = 0;
   if (push) {
     // Every rank's view is ready to be written (its gaps cleared, its earlier loads done).
     if ((st = nccl_barrier(g, deadline)) != TCX_OK) return st;
+    TCX_CUDA_TRY(cudaEventRecord(g->ev_push, g->s_comm));
+    // The pushes run on the copy engines, one stream per peer: no SM time is
+    // taken from the leaf hash that is still running, and the peers' transfers
+    // proceed side by side. A job is one 2-D copy (rows at the source and
+    // destination pitches) from the staged range straight into the peer's view.
     for (int p = 0; p < world; ++p) {
-      const uint64_t n = push_off[p + 1] - push_off[p];
-      if (p == rank || n == 0) continue;
+      if (p == rank || push_off[p + 1] == push_off[p]) continue;
+      cudaStream_t sp = g->s_peer[p];
+      TCX_CUDA_TRY(cudaStreamWaitEvent(sp, g->ev_push, 0));
       uint8_t* peer_view = static_cast<uint8_t*>(g->peer_views[p].base) + g->peer_views[p].offset;
-      if ((st = launch_copy_jobs(stage, peer_view, dj + o_push + push_off[p], n, prefix_for(n), g->s_comm, true,
-                                 load_copy_ctas())) != TCX_OK)
-        return st;
+      for (uint64_t i = push_off[p]; i < push_off[p + 1]; ++i) {
+        const tcx_copy_job& j = push_jobs[i];
+        if (j.rows == 0 || j.row_bytes == 0) continue;
+        if (j.rows == 1)
+          TCX_CUDA_TRY(cudaMemcpyAsync(peer_view + j.dst_off, stage + j.src_off, j.row_bytes, cudaMemcpyDeviceToDevice, sp));
+        else
+          TCX_CUDA_TRY(cudaMemcpy2DAsync(peer_view + j.dst_off, j.dst_pitch, stage + j.src_off, j.src_pitch, j.row_bytes,
+                                         j.rows, cudaMemcpyDeviceToDevice, sp));
+      }
+      TCX_CUDA_TRY(cudaEventRecord(g->peer_done[p], sp));
+      TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->peer_done[p], 0));
     }
     // Every peer has finished writing into this rank's view.
     if ((st = nccl_barrier(g, deadline)) != TCX_OK) return st;
@@ -695,7 +734,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     if (k >= 2) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->sent_events[k - 2], 0));
     const uint64_t np = pack_off[k + 1] - pack_off[k];
     if (np && (st = launch_copy_jobs(stage, g->send.p, dj + o_pack + pack_off[k], np,
-                                     prefix_for(np), g->s_pack, false, load_copy_ctas())) != TCX_OK)
+                                     prefix_for(np), g->s_pack, load_copy_ctas(n_mine))) != TCX_OK)
       return st;
     TCX_CUDA_TRY(cudaEventRecord(g->packed_events[k], g->s_pack));
     TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[k], 0));
@@ -722,7 +761,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
     const uint64_t ns = scat_off[k + 1] - scat_off[k];
     if (ns && (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter + scat_off[k], ns,
-                                     prefix_for(ns), g->s_comm, false, load_copy_ctas())) != TCX_OK)
+                                     prefix_for(ns), g->s_comm, load_copy_ctas(n_mine))) != TCX_OK)
       return st;
   }
   for (uint64_t i = 0; i < plan->n_permutes; ++i) {

@@ -22,11 +22,10 @@ void clear_error();
 void note_launches(uint64_t n);
 
 // Kernel launchers shared between translation units (stream-ordered).
-// remote_dst: d_dst is a peer GPU's memory (the kernel ends with a system-scope fence).
 // max_ctas: cap on the persistent grid (0: 8 CTAs per SM), for copies that run
 // beside other kernels.
 tcx_status launch_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* d_jobs, uint64_t n_jobs,
-                            uint64_t* d_prefix, cudaStream_t stream, bool remote_dst = false, uint32_t max_ctas = 0);
+                            uint64_t* d_prefix, cudaStream_t stream, uint32_t max_ctas = 0);
 int sm_count();
 tcx_status launch_permute(const void* d_src, void* d_dst, const tcx_permute_job& pj, cudaStream_t stream);
 tcx_status check_permute(const tcx_permute_job& pj);

@@ -73,8 +73,7 @@ __device__ __forceinline__ uint64_t find_job(const uint64_t* prefix, uint64_t n,
 __global__ void __launch_bounds__(kCopyThreads) copy_jobs_kernel(const uint8_t* __restrict__ src,
                                                                  uint8_t* __restrict__ dst,
                                                                  const tcx_copy_job* __restrict__ jobs, uint64_t n,
-                                                                 const uint64_t* __restrict__ prefix,
-                                                                 bool remote_dst) {
+                                                                 const uint64_t* __restrict__ prefix) {
   __shared__ uint64_t s_job;
   const uint64_t total = prefix[n];
   for (uint64_t w = blockIdx.x; w < total; w += gridDim.x) {
@@ -125,14 +124,6 @@ __global__ void __launch_bounds__(kCopyThreads) copy_jobs_kernel(const uint8_t* 
         dst[j.dst_off + row * j.dst_pitch + col] = src[j.src_off + row * j.src_pitch + col];
       }
     }
-  }
-  // A destination in a peer GPU's memory: after the CTA's barrier one thread's
-  // system-scope fence (cumulative over the writes the barrier ordered before it)
-  // makes the CTA's stores visible to the peer before the kernel ends; the
-  // barrier that follows on the host side then orders them for the peer.
-  if (remote_dst) {
-    __syncthreads();
-    if (threadIdx.x == 0) __threadfence_system();
   }
 }
 
@@ -365,7 +356,7 @@ int sm_count() {
 }
 
 tcx_status launch_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* d_jobs, uint64_t n_jobs,
-                            uint64_t* d_prefix, cudaStream_t stream, bool remote_dst, uint32_t max_ctas) {
+                            uint64_t* d_prefix, cudaStream_t stream, uint32_t max_ctas) {
   if (n_jobs == 0) return TCX_OK;
   copy_prefix_kernel<<<1, 1024, 0, stream>>>(d_jobs, n_jobs, d_prefix);
   note_launches(1);
@@ -373,7 +364,7 @@ tcx_status launch_copy_jobs(const void* d_src, void* d_dst, const tcx_copy_job* 
   unsigned grid = static_cast<unsigned>(sm_count()) * 8u;
   if (max_ctas) grid = std::min<unsigned>(grid, max_ctas);
   copy_jobs_kernel<<<grid, kCopyThreads, 0, stream>>>(static_cast<const uint8_t*>(d_src),
-                                                      static_cast<uint8_t*>(d_dst), d_jobs, n_jobs, d_prefix, remote_dst);
+                                                      static_cast<uint8_t*>(d_dst), d_jobs, n_jobs, d_prefix);
   note_launches(1);
   TCX_CUDA_TRY(cudaGetLastError());
   return TCX_OK;

@@ -170,7 +170,7 @@ class Group:
              view_hash: bool = False, peer_push: bool = False, target_ranges=None) -> dict:
         """Runs one load; returns the result fields as a dict. h_stage None: device-resident.
 
-        peer_push: exchange by writing into the peers' views over NVLink (d_view must be a
+        peer_push: exchange by copying into the peers' views over NVLink (d_view must be a
         cudaMalloc allocation of this process, e.g. a torch CUDA tensor); else NCCL send/recv.
         target_ranges: (offset, length) pairs of separate target tensors (TCX_LOAD_TARGETS):
         d_view is then the lowest target's address and view offsets are relative to it."""
