@@ -47,13 +47,15 @@ using Clock = std::chrono::steady_clock;
 constexpr uint64_t kDefaultSlab = 256 * 1024;
 constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchange round
 
-// Copy kernels of a load run while the leaf hash is still going. With fewer
-// chains than about one consumer warp per SMSP the hash is bound by each
-// warp's own instruction issue, and a full 8-CTA-per-SM copy grid sharing those
-// SMSPs slows every chain (measured: the 70B TP-4 hash went from about 80 to
-// 135 ms); a quarter of the SMs' worth of CTAs still moves several hundred GB/s
-// over NVLink or HBM. With more chains than that the hash is throughput-bound
-// like the copies, and the copies keep the full grid.
+// The local extraction copy of a load runs while the leaf hash is still going.
+// With fewer chains than about one consumer warp per SMSP the hash is bound by
+// each warp's own instruction issue, and a full 8-CTA-per-SM copy grid sharing
+// those SMSPs slows every chain (measured with the same grid pushing to peers:
+// the 70B TP-4 hash went from about 74 to 135 ms); a quarter of the SMs' worth
+// of CTAs still copies several hundred GB/s within HBM. With more chains than
+// that the hash is throughput-bound like the copy, which keeps the full grid.
+// (The NCCL path's pack and scatter kernels keep the full grid: they gate the
+// exchange, which is the longer leg of the 70B loads at N=2 and 4.)
 uint32_t load_copy_ctas(uint64_t n_chains) {
   const uint64_t sms = static_cast<uint64_t>(sm_count());
   return n_chains < sms * 128 ? static_cast<uint32_t>(std::max<uint64_t>(8, sms / 4)) : 0u;
@@ -734,7 +736,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     if (k >= 2) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->sent_events[k - 2], 0));
     const uint64_t np = pack_off[k + 1] - pack_off[k];
     if (np && (st = launch_copy_jobs(stage, g->send.p, dj + o_pack + pack_off[k], np,
-                                     prefix_for(np), g->s_pack, load_copy_ctas(n_mine))) != TCX_OK)
+                                     prefix_for(np), g->s_pack)) != TCX_OK)
       return st;
     TCX_CUDA_TRY(cudaEventRecord(g->packed_events[k], g->s_pack));
     TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[k], 0));
@@ -761,7 +763,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
     const uint64_t ns = scat_off[k + 1] - scat_off[k];
     if (ns && (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter + scat_off[k], ns,
-                                     prefix_for(ns), g->s_comm, load_copy_ctas(n_mine))) != TCX_OK)
+                                     prefix_for(ns), g->s_comm)) != TCX_OK)
       return st;
   }
   for (uint64_t i = 0; i < plan->n_permutes; ++i) {
