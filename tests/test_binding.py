@@ -191,3 +191,40 @@ def test_bind_into_rejects_bad_targets(cuda_device, artifact):
         art.bind_into({"model.norm.weight": torch.empty(64, dtype=torch.bfloat16, device="cuda")})
     with pytest.raises(api.ArtifactError, match="packing must be"):
         art.bind_into({"model.norm.weight": torch.empty(128, dtype=torch.bfloat16, device="cuda")}, packing="x")
+
+
+def test_mapped_copy_jobs_three_d_and_scalars(tmp_path):
+    """Dim-1 slices of a 3-D tensor (rows of slice x inner elements), a scalar and a 1-D
+    split, applied in numpy: every target equals torch slicing of the source."""
+    import json as _json
+    import struct
+    tensors = {"w3": torch.arange(4 * 6 * 5, dtype=torch.int32).view(4, 6, 5),
+               "s": torch.tensor(7, dtype=torch.int32), "v": torch.arange(10, dtype=torch.int32)}
+    hdr, payload, off = {}, b"", 0
+    for n in sorted(tensors):
+        b = tensors[n].numpy().tobytes()
+        hdr[n] = {"dtype": "I32", "shape": list(tensors[n].shape), "data_offsets": [off, off + len(b)]}
+        payload += b
+        off += len(b)
+    raw = _json.dumps(hdr).encode()
+    raw += b" " * ((8 - (8 + len(raw)) % 8) % 8)
+    path = tmp_path / "t.safetensors"
+    path.write_bytes(struct.pack("<Q", len(raw)) + raw + payload)
+    index = build_canonical_index(build_source_index([str(path)]))
+    canon = np.zeros(index.total_bytes, np.uint8)
+    for n, e in index.entries.items():
+        canon[e.offset:e.offset + e.size] = np.frombuffer(tensors[n].numpy().tobytes(), np.uint8)
+    mem = torch.zeros(1 << 14, dtype=torch.uint8)
+    a = mem[0:4 * 2 * 5 * 4].view(torch.int32).view(4, 2, 5)
+    b = mem[1024:1024 + 4 * 4 * 5 * 4].view(torch.int32).view(4, 4, 5)
+    sc = mem[4096:4100].view(torch.int32).view(())
+    v = mem[8192:8192 + 40].view(torch.int32)
+    targets = {"a": a, "b": b, "sc": sc, "v": v}
+    plan = [CopyPlanEntry("w3", Range(1, 0, 2), "a", None), CopyPlanEntry("w3", Range(1, 2, 6), "b", None),
+            CopyPlanEntry("s", None, "sc", None), CopyPlanEntry("v", Range(0, 5, 10), "v", Range(0, 0, 5)),
+            CopyPlanEntry("v", Range(0, 0, 5), "v", Range(0, 5, 10))]
+    validate_copy_plan(plan=plan, canonical_index=index,
+                       target_tensors={k: torch.empty_like(t) for k, t in targets.items()})
+    _apply(mapped_copy_jobs(plan, index, targets, mem.data_ptr()), canon, mem.numpy())
+    assert torch.equal(a, tensors["w3"][:, :2]) and torch.equal(b, tensors["w3"][:, 2:])
+    assert int(sc) == 7 and torch.equal(v, torch.cat([tensors["v"][5:], tensors["v"][:5]]))
