@@ -51,11 +51,12 @@ def parse_args():
     ap.add_argument("--leaf", type=int, default=LEAF)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", choices=["auto", "push", "nccl"], default="auto",
+    ap.add_argument("--exchange", choices=["auto", "push", "nccl", "allgather"], default="auto",
                     help="N>1 shard exchange: push over peer memory (copy-engine copies into the peers' views "
                          "over NVLink) or NCCL send/recv of packed windows; auto = push for the Llama-3-8B "
                          "artifact (its exchange hides behind the hash), NCCL for the 70B one (measured faster "
-                         "where the exchange is the longer leg)")
+                         "where the exchange is the longer leg); allgather = windowed broadcast of every rank's "
+                         "staged bytes to all ranks (every rank sees every byte)")
     ap.add_argument("--stage", choices=["mapped", "pinned"], default="pinned",
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
                          "(no second host copy), or a pinned copy read with parallel preads")
@@ -500,7 +501,8 @@ def main() -> None:
     def load(host: bool, expected=None):
         return group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage if host else None,
                           permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected,
-                          peer_push=exchange_mode(args) == "push" and world > 1)
+                          peer_push=exchange_mode(args) == "push" and world > 1,
+                          all_gather=exchange_mode(args) == "allgather" and world > 1)
 
     def max_over_ranks(x: float) -> float:
         if world == 1:
@@ -584,8 +586,10 @@ def main() -> None:
                              + (f"; {transposed} stored [in, out] and read whole through a transpose view"
                                 if transposed else "")),
                 "artifact_bytes": T, "leaf_bytes": L, "leaves": first["leaves"],
-                "exchange": ("push over peer memory (copy-engine 2-D copies into the peers' views over NVLink)"
-                             if exchange_mode(args) == "push" else "NCCL send/recv of packed windows") if world > 1 else "none",
+                "exchange": {"push": "push over peer memory (copy-engine 2-D copies into the peers' views over NVLink)",
+                             "nccl": "NCCL send/recv of packed windows",
+                             "allgather": "windowed all-gather (ncclBroadcast per root) + extraction"}[exchange_mode(args)]
+                if world > 1 else "none",
                 "view_bytes_per_rank": mine.view_bytes, "parallelism": f"tp{world}",
                 "l2": "inputs (staged bytes) far larger than the 126 MB L2; no flush needed",
                 "timing": "device events per step (tcx_group_load), mean over steps, max over ranks"},

@@ -292,6 +292,16 @@ typedef struct tcx_load_plan {
  * exchange and two one-word barriers. */
 #define TCX_LOAD_PEER_PUSH 2ull
 
+/* tcx_load_plan.flags: exchange by a windowed all-gather instead of the shard
+ * exchange: round k broadcasts every rank's staged bytes [bounds[r] + k*W,
+ * bounds[r] + (k+1)*W) to all ranks (W = window_bytes; one ncclBroadcast per
+ * root in one group) and each rank copies its view pieces out of the peers'
+ * windows. Every rank then has seen every byte (T*(N-1)/N received per rank),
+ * the reference's collective shape (collective_disk_loader.cc:4276-4554: chunks
+ * broadcast from their owner); the default shard exchange moves only each view's
+ * bytes. Excludes TCX_LOAD_PEER_PUSH. */
+#define TCX_LOAD_ALLGATHER 8ull
+
 /* tcx_load_plan.flags: the view is a set of separate caller tensors (the
  * reference's bind_into / mapped-target load, collective_disk_loader.cc:7909-8157,
  * 5818-6293): d_view is the lowest target's address, view offsets are device

@@ -559,9 +559,53 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     push_off[world] = push_jobs.size();
   }
 
+  // Windowed all-gather exchange: round k broadcasts every rank's staged bytes
+  // [b[r] + k*W, b[r] + (k+1)*W) to all ranks (one ncclBroadcast per root in a
+  // group, the root's own range in place), and each rank copies its view pieces
+  // out of every peer's window. Every rank receives every byte (T·(N-1)/N per
+  // rank instead of only its view's bytes).
+  const bool gather_all = world > 1 && (plan->flags & TCX_LOAD_ALLGATHER) != 0;
+  if (gather_all && push) return set_error(TCX_INVALID_ARGUMENT, "TCX_LOAD_ALLGATHER and TCX_LOAD_PEER_PUSH exclude each other");
+  uint64_t ag_rounds = 0, ag_slot = 0;
+  std::vector<uint64_t> ag_off;
+  std::vector<tcx_copy_job> ag_jobs;
+  auto ag_count = [&](int r, uint64_t k) -> uint64_t {
+    const uint64_t w0 = b[r] + k * W;
+    return w0 >= b[r + 1] ? 0 : std::min(W, b[r + 1] - w0);
+  };
+  if (gather_all) {
+    rounds = 0;
+    round_pack.clear();
+    round_scatter.clear();
+    std::fill(pack_off.begin(), pack_off.end(), 0);
+    std::fill(scat_off.begin(), scat_off.end(), 0);
+    uint64_t max_stage = 0;
+    for (int r = 0; r < world; ++r) max_stage = std::max(max_stage, b[r + 1] - b[r]);
+    ag_rounds = (max_stage + W - 1) / W;
+    ag_slot = std::min(W, std::max<uint64_t>(max_stage, 1));
+    ag_off.assign(ag_rounds + 1, 0);
+    const tcx_copy_job* my_jobs = plan->jobs + plan->job_offsets[rank];
+    const uint64_t n_my = plan->job_offsets[rank + 1] - plan->job_offsets[rank];
+    for (uint64_t k = 0; k < ag_rounds; ++k) {
+      for (int r = 0; r < world; ++r) {
+        const uint64_t n = ag_count(r, k);
+        if (r == rank || n == 0) continue;
+        const uint64_t w0 = b[r] + k * W;
+        tmp.clear();
+        clip_jobs(my_jobs, n_my, w0, w0 + n, tmp);
+        for (auto j : tmp) {
+          j.src_off = j.src_off - w0 + ((k % 2) * static_cast<uint64_t>(world) + static_cast<uint64_t>(r)) * ag_slot;
+          ag_jobs.push_back(j);
+        }
+      }
+      ag_off[k + 1] = ag_jobs.size();
+    }
+  }
+
   // --- buffers --------------------------------------------------------------
-  const uint64_t n_jobs_all = round_pack.size() + local_kept.size() + round_scatter.size() + compact.size();
-  const uint64_t n_launches = 2 * rounds + 2;
+  const uint64_t n_jobs_all =
+      round_pack.size() + local_kept.size() + round_scatter.size() + compact.size() + ag_jobs.size();
+  const uint64_t n_launches = 2 * rounds + 2 + ag_rounds;
   if ((st = g->digests_mine.grow(std::max<uint64_t>(max_n, 1) * 32)) != TCX_OK) return st;
   if ((st = g->states.grow(std::max<uint64_t>(n_mine, 1) * 32)) != TCX_OK) return st;
   if ((st = g->merkle_scratch.grow(merkle_scratch_bytes(n_total))) != TCX_OK) return st;
@@ -572,6 +616,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   if (rounds && max_recv_buf && (st = g->recv.grow(2 * peers.size() * recv_slot)) != TCX_OK) return st;
   if (perm_bytes && (st = g->perm_scratch.grow(perm_bytes)) != TCX_OK) return st;
   if (push && (st = g->barrier_word.grow(256)) != TCX_OK) return st;
+  if (ag_rounds && (st = g->recv.grow(2 * static_cast<uint64_t>(world) * ag_slot)) != TCX_OK) return st;
   if (world > 1) {
     if ((st = g->digests_all.grow(static_cast<uint64_t>(world) * max_n * 32)) != TCX_OK) return st;
     if ((st = g->digests_compact.grow(n_total * 32)) != TCX_OK) return st;
@@ -584,8 +629,8 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
     if ((st = g->view_digests.grow(view_n * 32)) != TCX_OK) return st;
     if ((st = g->view_scratch.grow(merkle_scratch_bytes(view_n) + 256)) != TCX_OK) return st;
   }
-  if ((st = ensure_events(g->packed_events, rounds)) != TCX_OK) return st;
-  if ((st = ensure_events(g->sent_events, rounds)) != TCX_OK) return st;
+  if ((st = ensure_events(g->packed_events, std::max(rounds, ag_rounds))) != TCX_OK) return st;
+  if ((st = ensure_events(g->sent_events, std::max(rounds, ag_rounds))) != TCX_OK) return st;
   if (n_jobs_all > g->h_jobs_cap) {
     if (g->h_jobs) cudaFreeHost(g->h_jobs);
     g->h_jobs = nullptr;
@@ -595,11 +640,12 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   }
   tcx_copy_job* hj = g->h_jobs;
   const uint64_t o_pack = 0, o_local = round_pack.size(), o_scatter = o_local + local_kept.size(),
-                 o_compact = o_scatter + round_scatter.size();
+                 o_compact = o_scatter + round_scatter.size(), o_ag = o_compact + compact.size();
   std::copy(round_pack.begin(), round_pack.end(), hj + o_pack);
   std::copy(local_kept.begin(), local_kept.end(), hj + o_local);
   std::copy(round_scatter.begin(), round_scatter.end(), hj + o_scatter);
   std::copy(compact.begin(), compact.end(), hj + o_compact);
+  std::copy(ag_jobs.begin(), ag_jobs.end(), hj + o_ag);
   auto* dj = static_cast<tcx_copy_job*>(g->jobs.p);
   auto* dprefix = static_cast<uint64_t*>(g->prefix.p);
   // Each copy-job launch gets its own prefix region, handed out in launch order
@@ -766,6 +812,30 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
                                      prefix_for(ns), g->s_comm)) != TCX_OK)
       return st;
   }
+  for (uint64_t k = 0; k < ag_rounds; ++k) {
+    // The window slots of round k were last read by the extraction of round k-2.
+    if (k >= 2) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[k - 2], 0));
+    if ((st = nccl_check(g, ncclGroupStart(), deadline, "ncclGroupStart")) != TCX_OK) return st;
+    for (int r = 0; r < world; ++r) {
+      const uint64_t n = ag_count(r, k);
+      if (n == 0) continue;
+      uint8_t* buf = r == rank ? stage + k * W
+                               : g->recv.bytes() + ((k % 2) * static_cast<uint64_t>(world) + static_cast<uint64_t>(r)) * ag_slot;
+      st = nccl_check(g, ncclBroadcast(buf, buf, n, ncclUint8, r, g->comm, g->s_comm), deadline, "ncclBroadcast");
+      if (st != TCX_OK) return st;
+      if (r == rank) sent += n * static_cast<uint64_t>(world - 1);
+      else received += n;
+    }
+    if ((st = nccl_check(g, ncclGroupEnd(), deadline, "exchange")) != TCX_OK) return st;
+    TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
+    TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->sent_events[k], 0));
+    const uint64_t ne = ag_off[k + 1] - ag_off[k];
+    if (ne && (st = launch_copy_jobs(g->recv.p, view, dj + o_ag + ag_off[k], ne, prefix_for(ne), g->s_pack,
+                                     load_copy_ctas(n_mine))) != TCX_OK)
+      return st;
+    TCX_CUDA_TRY(cudaEventRecord(g->packed_events[k], g->s_pack));
+  }
+  if (ag_rounds) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[ag_rounds - 1], 0));
   for (uint64_t i = 0; i < plan->n_permutes; ++i) {
     tcx_permute_job pj = plan->permutes[i];
     uint64_t bytes = pj.esize;

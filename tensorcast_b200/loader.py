@@ -21,6 +21,7 @@ from .views import JOB_DTYPE, permute_array
 VIEW_HASH = 1  # TCX_LOAD_VIEW_HASH
 PEER_PUSH = 2  # TCX_LOAD_PEER_PUSH
 TARGETS = 4  # TCX_LOAD_TARGETS
+ALLGATHER = 8  # TCX_LOAD_ALLGATHER
 
 
 def stage_bounds(total: int, leaf: int, world: int) -> list[int]:
@@ -167,18 +168,21 @@ class Group:
 
     def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, permutes=(), view_bytes=None,
              expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0,
-             view_hash: bool = False, peer_push: bool = False, target_ranges=None) -> dict:
+             view_hash: bool = False, peer_push: bool = False, target_ranges=None, all_gather: bool = False) -> dict:
         """Runs one load; returns the result fields as a dict. h_stage None: device-resident.
 
         peer_push: exchange by copying into the peers' views over NVLink (d_view must be a
-        cudaMalloc allocation of this process, e.g. a torch CUDA tensor); else NCCL send/recv.
+        cudaMalloc allocation of this process, e.g. a torch CUDA tensor); all_gather: a windowed
+        all-gather of every rank's staged bytes instead (every rank sees every byte); else the
+        NCCL send/recv shard exchange.
         target_ranges: (offset, length) pairs of separate target tensors (TCX_LOAD_TARGETS):
         d_view is then the lowest target's address and view offsets are relative to it."""
         if view_bytes is None:
             view_bytes = d_view.numel() * d_view.element_size() if isinstance(d_view, torch.Tensor) else 0
         plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes, window_bytes,
                      flags=(VIEW_HASH if view_hash else 0) | (PEER_PUSH if peer_push else 0) |
-                     (TARGETS if target_ranges is not None else 0), target_ranges=target_ranges)
+                     (TARGETS if target_ranges is not None else 0) | (ALLGATHER if all_gather else 0),
+                     target_ranges=target_ranges)
         res = _native.LoadResult()
         exp = None
         if expected_root is not None:

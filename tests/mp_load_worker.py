@@ -64,18 +64,22 @@ def main() -> int:
             d_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, device="cuda")
             d_view = torch.full((max(plan.view_bytes, 1),), 0x3C, dtype=torch.uint8, device="cuda")
             want_root = oracle.tree_root(oracle.leaf_digests(canon, leaf))
-            for host, window, push in ((True, 0, False), (False, 0, False), (False, 1000, False), (True, 4096, False),
-                                       (True, 0, True), (False, 0, True)):
+            for host, window, push, ag in ((True, 0, False, False), (False, 0, False, False),
+                                           (False, 1000, False, False), (True, 4096, False, False),
+                                           (True, 0, True, False), (False, 0, True, False),
+                                           (True, 0, False, True), (False, 3000, False, True)):
                 if not host:
                     d_stage[: hi - lo].copy_(torch.from_numpy(canon[lo:hi]).cuda())
                 d_view.fill_(0x3C)
                 res = group.load(canon.size, leaf, bounds, rank_jobs, d_stage=d_stage, d_view=d_view,
                                  h_stage=h if host else None, permutes=plan.permutes, view_bytes=plan.view_bytes,
-                                 expected_root=want_root, slab_bytes=256, window_bytes=window, peer_push=push)
+                                 expected_root=want_root, slab_bytes=256, window_bytes=window, peer_push=push,
+                                 all_gather=ag)
                 want = oviews.materialize_view(canon, meta, slices, transpose, subset)
                 got = d_view.cpu().numpy()[: plan.view_bytes]
                 if res["root"] != want_root or got.size != want.size or not (got == want).all():
-                    print(f"rank {rank}: case {name} host={host} window={window} push={push} FAILED", flush=True)
+                    print(f"rank {rank}: case {name} host={host} window={window} push={push} all_gather={ag} FAILED",
+                          flush=True)
                     failures += 1
         # Separate target tensors (bind_into, TCX_LOAD_TARGETS) over the NCCL exchange:
         # the Llama TP views with every tensor in its own allocation, guard bytes around.
