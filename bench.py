@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tcx|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
 
-Workload (BASELINE configs[1] at N=1, its tensor-parallel form at N>1): a synthetic
+Workload (the single-GPU load benchmark at N=1, its tensor-parallel form at N>1): a synthetic
 Llama-3-8B-shaped bf16 safetensors artifact (seed 1, 16 060 522 496 payload bytes) in
 tmpfs. Each rank stages its leaf-aligned 1/N of the canonical byte space, hashes the
 leaves it staged (SHA-256, explicit 4 MiB leaves), the ranks exchange over NVLink the
@@ -37,7 +37,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Realized GB/s into 1/2/4/8 B200 (SHA-256 verified); GPU SHA-256 GB/s/GPU"
 LEAF = 4 << 20
-SEEDS = {"llama3-8b": 1, "llama3-70b": 2}  # BASELINE configs 2 and 4
+SEEDS = {"llama3-8b": 1, "llama3-70b": 2}  # the 8B and 70B benchmark artifacts
 
 
 def parse_args():
@@ -61,7 +61,7 @@ def parse_args():
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
                          "(no second host copy), or a pinned copy read with parallel preads")
     ap.add_argument("--workload", choices=["artifact", "kv", "disk-hash"], default="artifact",
-                    help="artifact: the collective from-disk load (default); kv: BASELINE config 5, paged KV "
+                    help="artifact: the collective from-disk load (default); kv: the paged-KV benchmark, paged KV "
                          "gather + per-sequence hash, 8 sequence shards dealt to the ranks; disk-hash: "
                          "compute_data_multihash_from_disk_dir of the artifact's directory on one GPU, against "
                          "the reference's single-core CPU path")
@@ -171,7 +171,7 @@ TRANSPOSED_O_PROJ = "model.layers.0.self_attn.o_proj.weight"
 
 
 def model_shapes(model: str) -> dict:
-    """BASELINE shapes: Llama-3-8B (config 2/3) or Llama-3-70B (config 4, whose layer-0 o_proj is
+    """Benchmark shapes: Llama-3-8B (single-GPU and TP-8 loads) or Llama-3-70B (the 70B collective load, whose layer-0 o_proj is
     stored as [in, out] and read through a transpose view)."""
     from tensorcast_b200.synthetic import LLAMA3_70B, LLAMA3_8B, llama_shapes
     if model == "llama3-8b":
@@ -215,7 +215,7 @@ def ensure_artifact(args, rank: int, local_rank: int, world: int = 1) -> str:
 
 
 def tp_slices(index, world: int, rank: int) -> dict:
-    """BASELINE TP sharding: q/k/v/gate/up, embed and lm_head along dim 0; o/down along dim 1."""
+    """Tensor-parallel sharding of the benchmark: q/k/v/gate/up, embed and lm_head along dim 0; o/down along dim 1."""
     out = {}
     for name, e in index.entries.items():
         if any(k in name for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj", "embed_tokens", "lm_head")):
@@ -591,7 +591,7 @@ def main() -> None:
 
 
 def run_kv(args) -> None:
-    """64 planes (32 layers x K/V) of 65536 pages [16, 8, 128] bf16 (seed 3),
+    """The paged-KV benchmark: 64 planes (32 layers x K/V) of 65536 pages [16, 8, 128] bf16 (seed 3),
     sequences of 64-4096 tokens drawn in order until the pool is full, pages at a seeded
     permutation; the sequences are dealt to 8 shards and rank r processes shards r, r+N, ...
     (each shard's pool holds its own pages in their global random order). A step gathers

@@ -71,7 +71,7 @@ def materialize_view(canon: np.ndarray, meta: dict, slices=None, transpose=None,
 
 
 def tp_slices(meta: dict, world: int, rank: int) -> dict:
-    """The Llama tensor-parallel sharding of the BASELINE configs: q/k/v/gate/up, embed and
+    """The Llama tensor-parallel sharding of the benchmark loads: q/k/v/gate/up, embed and
     lm_head split along dim 0, o_proj/down_proj along dim 1, everything else whole."""
     out = {}
     for n, (_, shape, _) in meta.items():

@@ -1,4 +1,4 @@
-"""Paged KV-cache gather + per-sequence content hash.
+"""Paged KV-cache gather + per-sequence content hash (the paged-KV benchmark).
 
 No reference implementation exists for this step (the reference keeps engine-owned
 KV as opaque byte artifacts); it combines the same leaf hash / Merkle tree /
@@ -12,7 +12,7 @@ multihash as the artifact path (2 MiB leaves) with an on-device gather:
   (tcx_sha256_leaf_table) and reduces one Merkle root per sequence
   (tcx_merkle_roots_segmented).
 
-``workload`` builds the seeded BASELINE workload: sequence lengths drawn from
+``workload`` builds the seeded benchmark workload: sequence lengths drawn from
 ``default_rng(seed).integers(64, 4097)`` in order while their pages fit in the
 pool, page slots from ``default_rng(seed).permutation(pool_pages)``, sequences
 dealt round-robin to ranks.

@@ -9,7 +9,7 @@ Scheme (fixed, so every run and every machine writes the same bytes):
   order, which for an all-bf16 model is also the canonical order, so payload == canonical
   bytes (the loader checks this rather than assuming it);
 * ``transposed`` names are stored with their two dimensions swapped ([in, out]), as the
-  BASELINE 70B config asks for one o_proj.
+  70B benchmark stores one o_proj.
 Generation runs on CUDA when available (fast) and on the CPU otherwise; the two devices
 produce different (each deterministic) bytes, so fixtures record the device used.
 """

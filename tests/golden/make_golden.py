@@ -71,7 +71,7 @@ def main() -> None:
                           "root": root.hex(), "multihash": multihash(root)})
     out["small"] = cases
 
-    # 1 GiB, seed 0, 4 MiB leaves (256 digests) and the reference GPU
+    # the 1 GiB hash-parity case: seed 0, 4 MiB leaves (256 digests) and the reference GPU
     # policy's 512 KiB leaves (2048 digests).
     c1 = seeded_bytes(0, 1 << 30)
     c1_entries = []

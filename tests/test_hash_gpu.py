@@ -66,7 +66,7 @@ def test_reference_gpu_vs_cpu_64_bytes(cuda_device):
 
 
 def test_c1_1gib_golden_digests(cuda_device):
-    """BASELINE config 1 on the GPU: 256 x 4 MiB and 2048 x 512 KiB leaves of 1 GiB seed-0 bytes."""
+    """The 1 GiB hash-parity case on the GPU: 256 x 4 MiB and 2048 x 512 KiB leaves of 1 GiB seed-0 bytes."""
     with open(os.path.join(GOLDEN, "hash_golden.json")) as f:
         g = json.load(f)
     dev = to_dev(seeded(0, 1 << 30))

@@ -1,4 +1,4 @@
-"""Paged KV gather + per-sequence hash: workload construction on the
+"""Paged KV gather + per-sequence hash (the paged-KV benchmark): workload construction on the
 CPU, and on the GPU every gathered sequence and its multihash against the numpy/OpenSSL
 oracle (oracle/kv.py)."""
 import numpy as np

@@ -99,7 +99,7 @@ def test_leaf_policy_non_default_requests():
     assert oracle.determine_leaf_chunk_size(1 << 30, 0) == 4 << 20  # 0 != default: no halving
     assert oracle.determine_leaf_chunk_size(1 << 30, 128 << 20) == 64 << 20
     assert oracle.determine_leaf_chunk_size(1 << 30, 2 << 20) == 2 << 20
-    # BASELINE sizes: Llama-3-8B-shaped (16 060 522 496 B) and 70B-shaped artifacts
+    # benchmark sizes: Llama-3-8B-shaped (16 060 522 496 B) and 70B-shaped artifacts
     assert oracle.determine_leaf_chunk_size(16_060_522_496, 4 << 20) == 2 << 20
     assert oracle.determine_leaf_chunk_size(141_107_412_992, 4 << 20) == 4 << 20
 
@@ -120,7 +120,7 @@ def test_small_golden_cases():
 
 
 def test_c1_golden_1gib():
-    """1 GiB seed-0 bytes, 4 MiB leaves (256 digests) through the CPU path,
+    """The 1 GiB hash-parity case: seed-0 bytes, 4 MiB leaves (256 digests) through the CPU path,
     and the reference GPU policy's 512 KiB leaves (2048 digests)."""
     with open(os.path.join(GOLDEN, "hash_golden.json")) as f:
         g = json.load(f)
