@@ -308,8 +308,8 @@ typedef struct tcx_load_plan {
  * addresses relative to it, and target_ranges lists the writable (offset,
  * length) ranges. Every job and permute of this rank must lie inside one
  * target; bytes between targets are never touched (no gap zero-fill). Not
- * combinable with TCX_LOAD_VIEW_HASH or TCX_LOAD_PEER_PUSH (the exchange uses
- * NCCL send/recv). */
+ * combinable with TCX_LOAD_VIEW_HASH or TCX_LOAD_PEER_PUSH (the exchange is
+ * the NCCL send/recv shard exchange or TCX_LOAD_ALLGATHER). */
 #define TCX_LOAD_TARGETS 4ull
 
 /* Per-peer sizes and job lists of the exchange for one rank (host-only planning).
