@@ -113,3 +113,62 @@ def test_stage_bounds():
     assert b[0] == 0 and b[-1] == 16_060_522_496 and all(x % (4 << 20) == 0 for x in b[:-1])
     n = [(b[i + 1] - b[i] + (4 << 20) - 1) // (4 << 20) for i in range(8)]
     assert sum(n) == 3830 and max(n) - min(n) <= 1
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_exchange_schedule_into_sparse_targets(world):
+    """bind_into-style destinations: every view tensor relocated to its own place in a sparse
+    address space (gaps between targets). The schedule must fill each target exactly, with
+    direct receives only where a peer's bytes are contiguous in that space, and the bytes
+    between targets must stay untouched (no gap fill for target loads)."""
+    from types import SimpleNamespace
+
+    import torch
+
+    from tensorcast_b200.api import _TORCH_DTYPES
+    from tensorcast_b200.binding import target_ranges, view_target_jobs
+    for seed in range(4):
+        canon, meta = oviews.canonical_bytes(random_tensors(50 + seed, n=16))
+        index = index_from_meta(meta, canon.size)
+        rng = np.random.default_rng(seed)
+        leaf = 256
+        bounds = stage_bounds(canon.size, leaf, world)
+        views, plans, targets_all, sparse = [], [], [], []
+        for r in range(world):
+            slices, transpose, subset, spec = random_view(meta, rng)
+            plan = plan_view(index, spec, subset)
+            # one "allocation" per tensor inside a host arena, shuffled order, random gaps
+            arena = torch.zeros(plan.view_bytes * 3 + 4096 * len(plan.tensors), dtype=torch.uint8)
+            order = rng.permutation(len(plan.tensors))
+            cur, targets = 0, {}
+            for i in order:
+                t = plan.tensors[i]
+                cur += int(rng.integers(0, 64)) * 16
+                targets[t.name] = arena[cur:cur + t.nbytes].view(_TORCH_DTYPES[t.dtype]).view(t.shape)
+                cur = (cur + t.nbytes + 15) // 16 * 16
+            base, ranges, vbytes = target_ranges(targets)
+            jobs, perms = view_target_jobs(plan, targets, base)
+            views.append((slices, transpose, subset))
+            plans.append(SimpleNamespace(jobs=jobs, permutes=perms, view_bytes=vbytes))
+            targets_all.append((plan, targets, base))
+            sparse.append(ranges)
+        exch = [plan_exchange(canon.size, leaf, bounds, [p.jobs for p in plans], r, plans[r].view_bytes)
+                for r in range(world)]
+        got = emulate_load(canon, bounds, plans, exch)
+        for r in range(world):
+            plan, targets, base = targets_all[r]
+            want = oviews.materialize_view(canon, meta, *views[r])
+            for t in plan.tensors:
+                off = targets[t.name].data_ptr() - base
+                assert (got[r][off:off + t.nbytes] == want[t.offset:t.offset + t.nbytes]).all(), (seed, r, t.name)
+            # bytes outside every target: only the gap fill may have written them, and a
+            # target load skips the gap fill
+            covered = np.zeros(got[r].size, bool)
+            for a, n in sparse[r]:
+                covered[a:a + n] = True
+            written_outside = False
+            for p in range(world):
+                if p != r and exch[r]["direct"][p]:
+                    o, n = int(exch[r]["recv_view_off"][p]), int(exch[r]["recv_counts"][p])
+                    written_outside |= bool((~covered[o:o + n]).any())
+            assert not written_outside, (seed, r)
