@@ -446,7 +446,8 @@ typedef struct tcx_load_result {
  * after the work already queued on `stream` (the caller's stream, NULL = the
  * legacy default stream) and the call returns once it is complete.
  * expected_root (32 bytes, may be NULL): a mismatch returns DATA_LOSS
- * (verification_stage.cc:130-141). */
+ * (verification_stage.cc:130-141). Loads on one group run one at a time
+ * (concurrent calls wait); different groups are independent. */
 tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage, void* d_view,
                           const uint8_t* expected_root, tcx_load_result* out, void* stream);
 

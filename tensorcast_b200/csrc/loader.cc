@@ -29,6 +29,7 @@
 #include <cstdio>
 #include <chrono>
 #include <cstring>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -90,6 +91,7 @@ struct DevBuf {
 }  // namespace
 
 struct tcx_group {
+  std::mutex mu;  // one load at a time per group (the buffers and streams below are shared)
   int world = 1, rank = 0, device = 0;
   int64_t timeout_ms = 60000;
   ncclComm_t comm = nullptr;
@@ -409,6 +411,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
                                      void* d_view, const uint8_t* expected_root, tcx_load_result* out,
                                      void* stream) {
   if (g == nullptr) return set_error(TCX_INVALID_ARGUMENT, "group is null");
+  std::lock_guard<std::mutex> lock(g->mu);
   if (g->world > 1 && g->comm == nullptr)
     return set_error(TCX_FAILED_PRECONDITION, "group communicator was aborted by an earlier failure");
   tcx_status st = validate_load_plan(plan, g->world);
