@@ -540,6 +540,24 @@ def main() -> None:
     h2d_ms = max_over_ranks(statistics.mean(r["h2d_ms"] for r in e2e_res))
     peer = max_over_ranks(float(e2e_res[-1]["peer_recv_bytes"]))
 
+    # e2e bound: this run's own host-to-device rate, a plain pinned -> device copy of each
+    # rank's staged range on all ranks at once (the same bytes d_stage already holds).
+    h2d_peak = None
+    if isinstance(h_stage, torch.Tensor):
+        n = min(hi - lo, 4 << 30)
+        s = torch.cuda.current_stream()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = 0.0
+        for _ in range(3):
+            barrier()
+            c0.record(s)
+            d_stage[:n].copy_(h_stage[:n], non_blocking=True)
+            c1.record(s)
+            c1.synchronize()
+            t = max_over_ranks(c0.elapsed_time(c1))
+            best = max(best, n * world / t / 1e6)
+        h2d_peak = round(best, 2)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and canonical_is_payload:
         cpu = cpu_reference_sample(path, whole[0][1], T, L, args.cpu_seconds)
@@ -570,7 +588,11 @@ def main() -> None:
             "e2e": {"value": round(T / e2e_ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": hi - lo if world == 1 else T, "d2h_bytes_per_step": 32 * world,
                     "h2d_ms": round(h2d_ms, 3), "h2d_gbs_per_gpu": round((hi - lo) / h2d_ms / 1e6, 2),
-                    "gpu_launches": int(e2e_launches)},
+                    "gpu_launches": int(e2e_launches),
+                    "bound": {"kind": "aggregate host-to-device copy", "peak_gbs": h2d_peak,
+                              "frac": round(T / e2e_ms / 1e6 / h2d_peak, 4) if h2d_peak else None,
+                              "source": "measured in this run: pinned -> device copy of each rank's staged range, "
+                                        "all ranks at once, best of 3, max over ranks"}},
             "gpu_launches": int(launches),
             "wall_ms_per_step": round(wall, 3),
             "phases_ms": {"hash": round(hash_ms, 3), "exchange_and_view": round(exch_ms, 3),
