@@ -178,3 +178,59 @@ def test_load_from_registered_file_mapping(cuda_device, tmp_path):
         g.close()
         m.close()
         os.unlink(path)
+
+
+def _rect_job(src_cols, dst_cols, sr0, sr1, sc0, sc1, dr0, dc0, esize=1):
+    return (sr0 * src_cols * esize + sc0 * esize, dr0 * dst_cols * esize + dc0 * esize, src_cols * esize,
+            dst_cols * esize, (sc1 - sc0) * esize, sr1 - sr0)
+
+
+@pytest.mark.parametrize("case", ["4x6", "6x8_to_6x9"])
+def test_reference_rect2d_cases_into_target(cuda_device, case):
+    """collective_disk_loader_test.cc:707-900: rect2d copies of a U8 payload 0..n-1 into a
+    target pre-filled with 0xEE, through tcx_group_load with TCX_LOAD_TARGETS (the local
+    mapped-target load): the rectangles land exactly, every other byte stays 0xEE."""
+    if case == "4x6":
+        rows, cols, drows, dcols = 4, 6, 4, 6
+        rects = [(1, 3, 2, 5, 0, 1)]
+    else:
+        rows, cols, drows, dcols = 6, 8, 6, 9
+        rects = [(1, 3, 2, 6, 0, 1), (3, 6, 0, 3, 3, 5)]
+    payload = np.arange(rows * cols, dtype=np.uint8)
+    want = np.full((drows, dcols), 0xEE, np.uint8)
+    src2 = payload.reshape(rows, cols)
+    jobs = []
+    for sr0, sr1, sc0, sc1, dr0, dc0 in rects:
+        want[dr0:dr0 + sr1 - sr0, dc0:dc0 + sc1 - sc0] = src2[sr0:sr1, sc0:sc1]
+        jobs.append(_rect_job(cols, dcols, sr0, sr1, sc0, sc1, dr0, dc0))
+    jobs = np.array(jobs, dtype=JOB_DTYPE)
+    target = torch.full((drows * dcols,), 0xEE, dtype=torch.uint8, device="cuda")
+    d_stage = torch.empty(payload.size, dtype=torch.uint8, device="cuda")
+    g = Group(1, 0, 0)
+    try:
+        expected = oracle.tree_root(oracle.leaf_digests(payload, 64))
+        res = g.load(payload.size, 64, [0, payload.size], [jobs], d_stage=d_stage, d_view=target.data_ptr(),
+                     h_stage=pinned(payload), view_bytes=target.numel(), expected_root=expected,
+                     target_ranges=[(0, target.numel())])
+        assert res["root"] == expected
+        torch.cuda.synchronize()
+        assert (target.cpu().numpy().reshape(drows, dcols) == want).all()
+    finally:
+        g.close()
+
+
+def test_reference_replicated_case_into_target(cuda_device):
+    """collective_disk_loader_test.cc:492-590: a replicated U8[16] tensor (0x40..0x4F) copied
+    whole into a 16-byte target pre-filled with 0xEE."""
+    payload = (0x40 + np.arange(16)).astype(np.uint8)
+    target = torch.full((16,), 0xEE, dtype=torch.uint8, device="cuda")
+    d_stage = torch.empty(16, dtype=torch.uint8, device="cuda")
+    g = Group(1, 0, 0)
+    try:
+        jobs = np.array([(0, 0, 16, 16, 16, 1)], dtype=JOB_DTYPE)
+        g.load(16, 64, [0, 16], [jobs], d_stage=d_stage, d_view=target.data_ptr(), h_stage=pinned(payload),
+               view_bytes=16, target_ranges=[(0, 16)])
+        torch.cuda.synchronize()
+        assert (target.cpu().numpy() == payload).all()
+    finally:
+        g.close()
