@@ -92,3 +92,29 @@ def test_descriptor_verification(cuda_device, artifact, tmp_path):
         assert ei.value.status_code == "DATA_LOSS"
     finally:
         os.unlink(desc)
+
+
+def test_canonical_index_multi_file_and_float8(tmp_path):
+    """test_safetensors_loading.py:12-67: canonical offsets are coalesced by sorted tensor
+    name across files (not file order), and float8 dtypes map to the torch names."""
+    from safetensors.torch import save_file
+    from tensorcast_b200.artifact import build_canonical_index, build_source_index, safetensors_files
+    d = tmp_path / "st"
+    d.mkdir()
+    save_file({"t": torch.arange(256, dtype=torch.uint8)}, str(d / "weights.safetensors"))
+    idx = build_canonical_index(build_source_index(safetensors_files(str(d))))
+    e = idx.entries["t"]
+    assert (e.offset, e.size, list(e.shape), list(e.stride), e.dtype, e.storage_offset) == \
+        (0, 256, [256], [1], "torch.uint8", 0)
+    save_file({"u": torch.arange(16, dtype=torch.uint8)}, str(d / "extra.safetensors"))
+    idx = build_canonical_index(build_source_index(safetensors_files(str(d))))
+    assert [(n, e.offset, e.size) for n, e in idx.entries.items()] == [("t", 0, 256), ("u", 256, 16)]
+    f8 = tmp_path / "f8"
+    f8.mkdir()
+    save_file({"fp8_e4m3": torch.zeros(8, dtype=torch.float8_e4m3fn),
+               "fp8_e5m2": torch.ones(8, dtype=torch.float8_e5m2)}, str(f8 / "weights.safetensors"))
+    idx = build_canonical_index(build_source_index(safetensors_files(str(f8))))
+    assert idx.entries["fp8_e4m3"].dtype == "torch.float8_e4m3fn"
+    assert idx.entries["fp8_e5m2"].dtype == "torch.float8_e5m2"
+    assert (idx.entries["fp8_e4m3"].offset, idx.entries["fp8_e4m3"].size) == (0, 8)
+    assert (idx.entries["fp8_e5m2"].offset, idx.entries["fp8_e5m2"].size) == (8, 8)
