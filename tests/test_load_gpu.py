@@ -123,7 +123,9 @@ def test_single_rank_load_random_views(cuda_device, host):
             assert res["multihash"] == oracle.multihash(expected)
             want = oviews.materialize_view(canon, meta, slices, transpose, subset)
             assert (d_view.cpu().numpy()[: plan.view_bytes] == want).all()
-            # the view hash: the GPU entry's data multihash of the view bytes (adaptive leaf policy)
+            # the view hash: the GPU entry's data multihash of the view bytes (adaptive leaf policy),
+            # as view_hash_utils_test.cc:94-145 / store_engine_view_test.cc:93-161 pin it: equal to
+            # the CPU hash of the expected view bytes
             assert res["view_multihash"] == oracle.multihash_gpu_semantics(want)
     finally:
         g.close()
