@@ -7,6 +7,9 @@ Same names, arguments and error behaviour as the TensorCast SDK for this path:
 * ``Artifact.subset(names)`` / ``Artifact.view(*, slices=None, transpose=None)`` /
   ``Artifact.tensor_dict(*, device, options=None, ctx=None)``
   (tensorcast/api/store/artifact.py:1779, 1765-1776, 1509-1520)
+* ``Artifact.bind_into(target_tensors, *, mapping=None, packing=..., options=None, ctx=None)``
+  (tensorcast/api/store/artifact.py:1889-2110): the load writes straight into caller-owned
+  CUDA tensors, optionally through a copy plan (``binding.py``)
 * ``CallContext(collective=CollectiveLoadGroup(group_id, world_size, rank))``
   (tensorcast/api/context.py:13-18)
 
