@@ -51,6 +51,7 @@ def parse_args():
     ap.add_argument("--leaf", type=int, default=LEAF)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's own GPU kernel")
     ap.add_argument("--exchange", choices=["auto", "push", "nccl", "allgather"], default="auto",
                     help="N>1 shard exchange: push over peer memory (copy-engine copies into the peers' views "
                          "over NVLink) or NCCL send/recv of packed windows; auto = push for the Llama-3-8B "
@@ -434,9 +435,15 @@ def main() -> None:
     mine = plans[rank]
     rank_jobs = [p.jobs for p in plans]
 
-    # Staged bytes in page-locked host memory (setup, timed separately): the file's own
-    # tmpfs pages mapped and registered in place when the canonical bytes are one payload
-    # range, else a pinned copy assembled with parallel preads.
+    # This rank's staged range as file segments: the from-file loads read them inside the
+    # timed step (tcx_group_load_files). Reader threads: the CPUs this rank may use,
+    # shared evenly by the ranks of this host.
+    files_mine = canonical_segments(index, lo, hi)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    read_threads = max(2, min(32, len(os.sched_getaffinity(0)) // max(1, local_world)))
+    # Staged bytes in page-locked host memory as well (setup), for the from-pinned-memory
+    # form of e2e and the host-to-device bound: the file's own tmpfs pages mapped and
+    # registered in place when asked, else a pinned copy assembled with parallel preads.
     from tensorcast_b200.loader import FileMapping
     stage_kind, h_stage, t_pin = "pinned copy", None, 0.0
     t0 = time.perf_counter()
@@ -451,12 +458,14 @@ def main() -> None:
         t0 = time.perf_counter()
         h_stage = torch.empty(hi - lo, dtype=torch.uint8, pin_memory=True)
         t_pin = time.perf_counter() - t0
+        read_segments(files_mine, h_stage.data_ptr(), threads=read_threads)  # first touch of the pinned pages
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
-        read_segments(canonical_segments(index, lo, hi), h_stage.data_ptr(),
-                      threads=max(2, min(16, len(os.sched_getaffinity(0)))))
+        read_segments(files_mine, h_stage.data_ptr(), threads=read_threads)
+        t_read = time.perf_counter() - t0
         for off, ln in pad_ranges(index, lo, hi):
             h_stage[off:off + ln].zero_()
-        t_read = time.perf_counter() - t0
     else:
         t_read = t_map
     d_stage = torch.empty(hi - lo, dtype=torch.uint8, device="cuda")
@@ -470,8 +479,10 @@ def main() -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    def load(host: bool, expected=None):
-        return group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage if host else None,
+    def load(host: bool, expected=None, from_files: bool = False):
+        return group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view,
+                          h_stage=h_stage if host and not from_files else None,
+                          files=files_mine if from_files else None, read_threads=read_threads,
                           permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected,
                           peer_push=exchange_mode(args) == "push" and world > 1,
                           all_gather=exchange_mode(args) == "allgather" and world > 1)
@@ -483,9 +494,9 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # First load (from host memory, so it also fills d_stage for the device-resident steps)
+    # First load (from the files, so it also fills d_stage for the device-resident steps)
     # establishes the root; rank 0 checks it against the CPU oracle over the whole file.
-    first = load(True)
+    first = load(True, from_files=True)
     root = first["root"]
     parity = {}
     if rank == 0:
@@ -499,17 +510,22 @@ def main() -> None:
                       "oracle_seconds": round(time.perf_counter() - t0, 1), "multihash": first["multihash"]}
             if cpu_root != root:
                 raise SystemExit(f"PARITY FAILURE: GPU root {root.hex()} != CPU oracle {cpu_root.hex()}")
-    # Views: check a fixed sample of tensors against numpy slicing of the file.
-    view_ok = verify_view_sample(path, index, mine, d_view, world, rank, whole, transposed)
+    # Views: every byte of every rank's view against numpy slicing of the file.
+    view_ok, view_checked, view_tensors = verify_view_full(path, index, mine, d_view, world, rank, transposed)
+    straddling = straddling_tensors(index, bounds)
     if world > 1:
-        ok = torch.tensor([1 if view_ok else 0], device="cuda")
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-        view_ok = bool(ok.item())
+        ok = torch.tensor([1 if view_ok else 0, view_checked, view_tensors], dtype=torch.float64, device="cuda")
+        mn = ok.clone()
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        dist.all_reduce(ok, op=dist.ReduceOp.SUM)
+        view_ok, view_checked, view_tensors = bool(mn[0].item()), int(ok[1].item()), int(ok[2].item())
     if not view_ok:
         raise SystemExit("PARITY FAILURE: view bytes differ from numpy slicing of the artifact")
 
     # Hash-kernel roofline (device-resident, alone, CUDA events on the launching stream).
     hk = hash_kernel_roofline(d_stage, hi - lo, L, rank)
+    # The reference's own GPU kernel on the same bytes (rank 0 of a one-GPU run).
+    ref_gpu = reference_gpu_kernel(d_stage, hi - lo, L, hk) if world == 1 and not args.no_ref_gpu else None
 
     # value: device-resident loads.
     for _ in range(args.warmup):
@@ -528,7 +544,29 @@ def main() -> None:
     exch_ms = max_over_ranks(statistics.mean(r["exchange_ms"] for r in steps))
     wall = max_over_ranks(wall)
 
-    # e2e: from pinned host memory through tcx_group_load.
+    # e2e (headline): from the files through tcx_group_load_files -- preads into the
+    # pinned ring, H2D, hash, exchange, view and the 32-byte root read back, all inside
+    # each step -- timed with events on this stream around the K steps, max over ranks.
+    cur = torch.cuda.current_stream()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        load(True, root, from_files=True)
+    barrier()
+    n0 = _native.lib().tcx_kernel_launch_count()
+    w0 = time.perf_counter()
+    f0.record(cur)
+    file_res = [load(True, root, from_files=True) for _ in range(args.steps)]
+    f1.record(cur)
+    f1.synchronize()
+    file_wall = (time.perf_counter() - w0) / args.steps * 1e3
+    barrier()
+    file_launches = _native.lib().tcx_kernel_launch_count() - n0
+    file_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+    file_wall = max_over_ranks(file_wall)
+    file_read_ms = max_over_ranks(statistics.mean(r["stage_read_ms"] for r in file_res))
+    file_h2d_ms = max_over_ranks(statistics.mean(r["h2d_ms"] for r in file_res))
+
+    # e2e from pinned host memory (the staged range already read into pinned memory).
     for _ in range(args.warmup):
         load(True, root)
     barrier()
@@ -539,6 +577,9 @@ def main() -> None:
     e2e_ms = max_over_ranks(statistics.mean(r["total_ms"] for r in e2e_res))
     h2d_ms = max_over_ranks(statistics.mean(r["h2d_ms"] for r in e2e_res))
     peer = max_over_ranks(float(e2e_res[-1]["peer_recv_bytes"]))
+    read_gbs = None
+    if stage_kind == "pinned copy" and t_read > 0:
+        read_gbs = round(T / max_over_ranks(t_read) / 1e9, 2)
 
     # e2e bound: this run's own host-to-device rate, a plain pinned -> device copy of each
     # rank's staged range on all ranks at once (the same bytes d_stage already holds).
@@ -585,26 +626,47 @@ def main() -> None:
                 "timing": "device events per step (tcx_group_load), mean over steps, max over ranks"},
             "sha256_gbs_per_gpu": hk["achieved"],
             "roofline": hk,
-            "e2e": {"value": round(T / e2e_ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
-                    "h2d_bytes_per_step": hi - lo if world == 1 else T, "d2h_bytes_per_step": 32 * world,
-                    "h2d_ms": round(h2d_ms, 3), "h2d_gbs_per_gpu": round((hi - lo) / h2d_ms / 1e6, 2),
-                    "gpu_launches": int(e2e_launches),
-                    "bound": {"kind": "aggregate host-to-device copy", "peak_gbs": h2d_peak,
-                              "frac": round(T / e2e_ms / 1e6 / h2d_peak, 4) if h2d_peak else None,
+            "e2e": {"value": round(T / file_ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(file_ms, 3),
+                    "from": f"the safetensors file in tmpfs (page-cache resident): {read_threads} reader threads per "
+                            "rank pread into a ring of pinned slots, H2D, hash, exchange, view, 32-byte root read "
+                            "back, all inside each step (tcx_group_load_files)",
+                    "h2d_bytes_per_step": T, "d2h_bytes_per_step": 32 * world,
+                    "stage_read_ms": round(file_read_ms, 3), "h2d_ms": round(file_h2d_ms, 3),
+                    "wall_ms_per_step": round(file_wall, 3), "gpu_launches": int(file_launches),
+                    "read_threads_per_rank": read_threads,
+                    "bound": {"kind": "aggregate host-to-device copy (and the host pread rate beside it)",
+                              "peak_gbs": h2d_peak,
+                              "frac": round(T / file_ms / 1e6 / h2d_peak, 4) if h2d_peak else None,
+                              "read_gbs": read_gbs,
+                              "frac_of_min_h2d_read": round(T / file_ms / 1e6 / min(h2d_peak, read_gbs), 4)
+                              if h2d_peak and read_gbs else None,
                               "source": "measured in this run: pinned -> device copy of each rank's staged range, "
-                                        "all ranks at once, best of 3, max over ranks"}},
+                                        "all ranks at once, best of 3, max over ranks; read_gbs: parallel preads of "
+                                        "each rank's range from the file into pinned memory (same threads), "
+                                        "all ranks at once"},
+                    "from_pinned": {
+                        "value": round(T / e2e_ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
+                        "h2d_ms": round(h2d_ms, 3), "h2d_gbs_per_gpu": round((hi - lo) / h2d_ms / 1e6, 2),
+                        "gpu_launches": int(e2e_launches),
+                        "frac_of_h2d": round(T / e2e_ms / 1e6 / h2d_peak, 4) if h2d_peak else None,
+                        "note": "the staged range already in pinned host memory (read before the step)"}},
             "gpu_launches": int(launches),
             "wall_ms_per_step": round(wall, 3),
             "phases_ms": {"hash": round(hash_ms, 3), "exchange_and_view": round(exch_ms, 3),
                           "note": "device-resident steps; hashing and the exchange run concurrently"},
             "peer_recv_bytes_per_rank": int(peer),
             "setup": {"host_stage": stage_kind, "stage_prep_s": round(t_read + t_pin, 2),
+                      "host_nproc": os.cpu_count(), "affinity_cpus": len(os.sched_getaffinity(0)),
                       "canonical_is_payload": canonical_is_payload, "local_cpus_bound": n_local_cpus},
-            "parity": dict(parity, view_sample_ok=view_ok),
+            "parity": dict(parity, view_full_ok=view_ok, view_bytes_checked=int(view_checked),
+                           view_tensors_checked=int(view_tensors), tensors_straddling_stage_bounds=straddling,
+                           view_check="every byte of every rank's view == numpy slicing of the file"),
             "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if ref_gpu is not None:
+            line["reference_gpu_kernel"] = ref_gpu
         print(json.dumps(line), flush=True)
     group.close()
     if world > 1:
@@ -735,33 +797,123 @@ def run_kv(args) -> None:
         dist.destroy_process_group()
 
 
-def verify_view_sample(path, index, plan, d_view, world, rank, whole, transposed=None) -> bool:
-    """Compares a deterministic sample of view tensors with numpy slicing of the file."""
+def verify_view_full(path, index, plan, d_view, world, rank, transposed=None):
+    """Compares every tensor of this rank's view, byte for byte, with numpy slicing of the
+    file (the tensor-parallel rule of tp_slices; the transposed tensor read whole and
+    transposed). Returns (ok, bytes checked, tensors checked)."""
     import numpy as np
     import torch
-    names = [t.name for t in plan.tensors]
-    pick = set(names[::37]) | {n for n in names if "embed" in n or "lm_head" in n or "layers.0." in n}
-    src = {n: index.sources[n] for n in pick}
-    ok = True
-    for t in plan.tensors:
-        if t.name not in pick:
-            continue
-        st = src[t.name]
-        arr = np.memmap(path, dtype=np.uint16, mode="r", offset=st.file_offset, shape=st.shape)
+    from concurrent.futures import ThreadPoolExecutor
+    from tensorcast_b200.artifact import ELEMENT_SIZE
+    slices = {} if world == 1 else tp_slices(index, world, rank)
+    udt = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}
+    torch.cuda.synchronize()
+
+    def check(t):
+        st, e = index.sources[t.name], index.entries[t.name]
+        es = ELEMENT_SIZE[e.dtype]
+        arr = np.memmap(path, dtype=udt[es], mode="r", offset=st.file_offset, shape=tuple(st.shape))
         if t.name == transposed:
             arr = arr.T
-        elif world > 1:
-            e = index.entries[t.name]
-            if any(k in t.name for k in ("o_proj", "down_proj")):
-                ln = e.shape[1] // world
-                arr = arr[:, rank * ln:(rank + 1) * ln]
-            elif any(k in t.name for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj", "embed", "lm_head")):
-                ln = e.shape[0] // world
-                arr = arr[rank * ln:(rank + 1) * ln]
+        elif t.name in slices:
+            d, sl = slices[t.name]
+            arr = arr[sl] if d == 0 else arr[:, sl]
+        want = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
         got = d_view[t.offset:t.offset + t.nbytes].cpu().numpy()
-        ok &= bool((got == np.ascontiguousarray(arr).view(np.uint8).reshape(-1)).all())
+        return bool(got.size == want.size and np.array_equal(got, want)), int(t.nbytes)
+
+    with ThreadPoolExecutor(max(2, min(16, len(os.sched_getaffinity(0))))) as ex:
+        res = list(ex.map(check, plan.tensors))
+    return all(r[0] for r in res), sum(r[1] for r in res), len(res)
+
+
+def straddling_tensors(index, bounds) -> int:
+    """Tensors whose canonical bytes cross a rank's stage boundary (their pieces come from two ranks)."""
+    inner = bounds[1:-1]
+    return sum(1 for e in index.entries.values() if any(e.offset < b < e.offset + e.size for b in inner))
+
+
+def reference_gpu_kernel(d_stage, nbytes: int, leaf: int, hk: dict):
+    """Times the reference's own GPU kernel (tensorcast_sha256_leaf_kernel, its source text
+    compiled with NVRTC for compute_100 by oracle/ref_gpu_build.py and launched with the
+    reference's configuration by oracle/_ref/libref_gpu.so) beside the product kernel on the
+    same bytes: the staged artifact at the bench's leaf size, and BASELINE config 1 (1 GiB of
+    seed-0 bytes) at the reference GPU policy's 512 KiB leaves, whose digests must equal the
+    committed golden ones. A baseline leg, like cpu_baseline."""
+    import ctypes
+    import numpy as np
+    import torch
+    import tensorcast_b200 as tcx
+    lib_path = os.path.join(ROOT, "oracle", "_ref", "libref_gpu.so")
+    ptx = os.path.join(ROOT, "oracle", "_ref", "tensorcast_sha256_compute_100.ptx")
+    if not (os.path.exists(lib_path) and os.path.exists(ptx)):
+        return {"unavailable": "oracle/_ref not built (make -C oracle ref needs the reference source tree)"}
+    lib = ctypes.CDLL(lib_path)
+    lib.ref_gpu_last_error.restype = ctypes.c_char_p
+    lib.ref_gpu_sha256_leaves.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_void_p,
+                                          ctypes.c_uint32, ctypes.c_void_p]
     torch.cuda.synchronize()
-    return ok
+    if lib.ref_gpu_load(ptx.encode(), torch.cuda.current_device()) != 0:
+        return {"unavailable": "reference kernel load failed: " + lib.ref_gpu_last_error().decode()}
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            e0.record(s)
+            fn()
+            e1.record(s)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    def ref_run(src, total, lf, out):
+        n = (total + lf - 1) // lf
+        rc = lib.ref_gpu_sha256_leaves(src.data_ptr(), total, lf, out.data_ptr(), n, s.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(lib.ref_gpu_last_error().decode())
+
+    out = {"kernel": "tensorcast_sha256_leaf_kernel: the reference's source text (core/common/artifact_hash_gpu.cc:"
+                     "193-412) compiled by NVRTC for compute_100 with its own options and JIT-loaded by the driver; "
+                     "launch 512 threads x min(ceil(leaves/512), 8*SMs) (:771-781)", "cases": {}}
+    # (1) the staged artifact at the bench's leaf size
+    n = (nbytes + leaf - 1) // leaf
+    ref_d = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+    ours = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+    ms = timed(lambda: ref_run(d_stage, nbytes, leaf, ref_d), 1)
+    tcx.sha256_leaves(d_stage, leaf, ours, nbytes=nbytes, stream=s)
+    torch.cuda.synchronize()
+    blocks = leaf // 64 + 1
+    out["cases"]["artifact"] = {"bytes": nbytes, "leaf_bytes": leaf, "leaves": n, "ms": round(ms, 3),
+                                "gbs": round(nbytes / ms / 1e6, 2), "us_per_block": round(ms * 1e3 / blocks, 3),
+                                "tcx_ms": hk["kernel_ms"],
+                                "tcx_us_per_block": round(hk["kernel_ms"] * 1e3 / blocks, 4),
+                                "speedup_tcx_vs_reference": round(ms / hk["kernel_ms"], 2),
+                                "digests_equal_tcx": bool(torch.equal(ref_d, ours))}
+    del ref_d, ours
+    # (2) BASELINE config 1 at the reference GPU policy's leaf: 1 GiB of seed-0 bytes, 512 KiB leaves
+    golden = os.path.join(ROOT, "tests", "golden", "c1_seed0_1gib_leaf512kib.digests.bin")
+    c1 = torch.from_numpy(np.random.default_rng(0).integers(0, 256, size=1 << 30, dtype=np.uint8)).cuda()
+    lf, total = 512 << 10, 1 << 30
+    n = total // lf
+    ref_d = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+    ours = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+    ms = timed(lambda: ref_run(c1, total, lf, ref_d), 3)
+    t_ms = timed(lambda: tcx.sha256_leaves(c1, lf, ours, stream=s), 5)
+    want = np.fromfile(golden, dtype=np.uint8).reshape(-1, 32) if os.path.exists(golden) else None
+    blocks = lf // 64 + 1
+    out["cases"]["c1_1GiB_512KiB"] = {
+        "bytes": total, "leaf_bytes": lf, "leaves": n, "ms": round(ms, 3), "gbs": round(total / ms / 1e6, 2),
+        "us_per_block": round(ms * 1e3 / blocks, 3), "tcx_ms": round(t_ms, 3),
+        "tcx_gbs": round(total / t_ms / 1e6, 2), "speedup_tcx_vs_reference": round(ms / t_ms, 2),
+        "reference_digests_equal_golden": None if want is None else bool((ref_d.cpu().numpy() == want).all()),
+        "tcx_digests_equal_golden": None if want is None else bool((ours.cpu().numpy() == want).all())}
+    del c1, ref_d, ours
+    torch.cuda.synchronize()
+    return out
 
 
 def hash_kernel_roofline(d_stage, nbytes: int, leaf: int, rank: int) -> dict:

@@ -160,13 +160,15 @@ tcx_status tcx_multihash_from_gpu(const void* d_src, uint64_t total_bytes, int d
  * that loads the library until the process exits. No counterpart in the
  * reference.
  * Same arguments, checks, leaf policy and result as tcx_multihash_from_gpu,
- * plus the stream the work runs on (NULL: the legacy default stream); returns
- * once the result is on the host. Limit: at most 16384 leaves per call (64 GiB
- * at the 4 MiB default leaf); more is INVALID_ARGUMENT.
+ * plus the stream the work runs on (NULL: the legacy default stream; otherwise
+ * a stream of device_id, else INVALID_ARGUMENT); returns once the result is on
+ * the host. The caller's current device is restored before it returns. Limit:
+ * at most 16384 leaves per call (64 GiB at the 4 MiB default leaf); more is
+ * INVALID_ARGUMENT.
  * The first call on a device finds the scratch array's device address; make
- * that first call before any stream capture. Calls on one device share the
- * scratch and are serialised by the library; work that overlaps them on the
- * GPU from elsewhere with the same scratch would race. */
+ * that first call before any stream capture. Calls
+ * on one device share the scratch and are serialised by the library; work that
+ * overlaps them on the GPU from elsewhere with the same scratch would race. */
 tcx_status tcx_multihash_from_gpu_noalloc(const void* d_src, uint64_t total_bytes, int device_id,
                                           uint64_t leaf_chunk_bytes, char* out, size_t out_capacity, void* stream);
 
@@ -437,6 +439,7 @@ typedef struct tcx_load_result {
   float h2d_ms, hash_ms, exchange_ms, total_ms;  /* device-timed phases on this rank */
   char view_multihash[64];  /* with TCX_LOAD_VIEW_HASH: data multihash of this rank's view, else "" */
   uint64_t view_leaf_bytes; /* leaf size used for view_multihash */
+  float stage_read_ms;      /* tcx_group_load_files: host time from the first read to the last slab read */
 } tcx_load_result;
 
 /* Runs one collective load on every rank of g (all ranks call it with the same
@@ -450,6 +453,29 @@ typedef struct tcx_load_result {
  * (concurrent calls wait); different groups are independent. */
 tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage, void* d_view,
                           const uint8_t* expected_root, tcx_load_result* out, void* stream);
+
+/* Where tcx_group_load_files reads this rank's staged range from. */
+typedef struct tcx_file_stage {
+  const tcx_file_segment* segments; /* the staged range [bounds[rank], bounds[rank+1]) as file ranges,
+                                       dst_offset relative to bounds[rank]; bytes no segment covers
+                                       are zero (the canonical space's alignment pads) */
+  uint64_t n_segments;
+  int read_threads;                 /* host reader threads (0: the CPUs the caller may run on, <= 32) */
+  int ring_slots;                   /* pinned slabs read ahead (0: 4) */
+  uint64_t slot_bytes;              /* pinned bytes per slab when plan->slab_bytes is 0 (0: 256 MiB) */
+} tcx_file_stage;
+
+/* tcx_group_load with the staged range read from files inside the call: the
+ * group's reader threads pread slab j (bytes [j*S, (j+1)*S) of every leaf of the
+ * range) into pinned slot j % ring_slots while earlier slabs are copied to
+ * d_stage and hashed, so reads, host-to-device copies and the streamed SHA-256
+ * passes overlap (the reference's read -> pinned -> H2D chunk loop with its
+ * two-deep ChunkPrefetcher, collective_disk_loader.cc:2277-2383, 5538-5816).
+ * The ring and the threads stay with the group for later loads. A file that
+ * cannot be opened is NOT_FOUND, a short read DATA_LOSS; total_ms then covers
+ * the reads as well. */
+tcx_status tcx_group_load_files(tcx_group* g, const tcx_load_plan* plan, const tcx_file_stage* files, void* d_stage,
+                                void* d_view, const uint8_t* expected_root, tcx_load_result* out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Paged KV-cache gather (no reference counterpart: the reference stores

@@ -90,7 +90,13 @@ class LoadResult(ctypes.Structure):
     _fields_ = [("root", _c.c_uint8 * 32), ("multihash", _c.c_char * 64), ("leaves", _c.c_uint64),
                 ("h2d_bytes", _c.c_uint64), ("peer_send_bytes", _c.c_uint64), ("peer_recv_bytes", _c.c_uint64),
                 ("h2d_ms", _c.c_float), ("hash_ms", _c.c_float), ("exchange_ms", _c.c_float),
-                ("total_ms", _c.c_float), ("view_multihash", _c.c_char * 64), ("view_leaf_bytes", _c.c_uint64)]
+                ("total_ms", _c.c_float), ("view_multihash", _c.c_char * 64), ("view_leaf_bytes", _c.c_uint64),
+                ("stage_read_ms", _c.c_float)]
+
+
+class FileStage(ctypes.Structure):
+    _fields_ = [("segments", _c.POINTER(FileSegment)), ("n_segments", _c.c_uint64), ("read_threads", _c.c_int),
+                ("ring_slots", _c.c_int), ("slot_bytes", _c.c_uint64)]
 
 
 # Every function exported by include/tcx.h with (restype, argtypes).
@@ -140,6 +146,8 @@ _SIGNATURES = {
     "tcx_group_destroy": (_c.c_int, [_c.c_void_p]),
     "tcx_group_load": (_c.c_int, [_c.c_void_p, _c.POINTER(LoadPlan), _c.c_void_p, _c.c_void_p, _c.c_void_p,
                                   _c.c_void_p, _c.POINTER(LoadResult), _c.c_void_p]),
+    "tcx_group_load_files": (_c.c_int, [_c.c_void_p, _c.POINTER(LoadPlan), _c.POINTER(FileStage), _c.c_void_p,
+                                        _c.c_void_p, _c.c_void_p, _c.POINTER(LoadResult), _c.c_void_p]),
 }
 
 

@@ -172,11 +172,16 @@ class Artifact:
         bounds = stage_bounds(T, L, world)
         lo, hi = bounds[rank], bounds[rank + 1]
         with torch.cuda.device(dev_index):
-            h_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, pin_memory=True)
-            read_segments(canonical_segments(self.index, lo, hi), h_stage.data_ptr(), threads=min(16, os.cpu_count() or 4),
-                          direct=bool(options and options.direct_io))
-            for off, ln in pad_ranges(self.index, lo, hi):
-                h_stage[off:off + ln].zero_()
+            # Buffered reads stream through the group's pinned ring inside the load
+            # (reads, copies and hashing overlap); O_DIRECT reads go through aligned
+            # windows into a pinned copy of the range first.
+            h_stage, files = None, canonical_segments(self.index, lo, hi)
+            if options and options.direct_io:
+                h_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, pin_memory=True)
+                read_segments(files, h_stage.data_ptr(), threads=min(16, os.cpu_count() or 4), direct=True)
+                for off, ln in pad_ranges(self.index, lo, hi):
+                    h_stage[off:off + ln].zero_()
+                files = None
             d_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, device=dev)
             if alias:
                 d_view = d_stage
@@ -189,10 +194,11 @@ class Artifact:
             group = _group_for(dev_index, world, rank, coll.group_id if coll else "")
             try:
                 res = group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage,
-                                 permutes=permutes, view_bytes=view_bytes, expected_root=expected,
+                                 files=files, permutes=permutes, view_bytes=view_bytes, expected_root=expected,
                                  target_ranges=target_ranges)
             except _native.TcxError as e:
-                code = {15: "DATA_LOSS", 3: "INVALID_ARGUMENT", 4: "DEADLINE_EXCEEDED"}.get(e.code, "INTERNAL")
+                code = {15: "DATA_LOSS", 3: "INVALID_ARGUMENT", 4: "DEADLINE_EXCEEDED",
+                        5: "NOT_FOUND"}.get(e.code, "INTERNAL")
                 raise ArtifactError(str(e), code) from e
         self.data_multihash = res["multihash"]
         res["d_view"] = d_view

@@ -85,6 +85,7 @@ struct FileHashContext {
         if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.hashed, cudaEventDisableTiming);
         if (e != cudaSuccess) {
+          cudaGetLastError();
           free_slots();
           return set_error(e == cudaErrorMemoryAllocation ? TCX_RESOURCE_EXHAUSTED : TCX_INTERNAL,
                            std::string("file hash buffers: ") + cudaGetErrorString(e));

@@ -26,10 +26,17 @@
 #include <algorithm>
 #include <atomic>
 #include <cctype>
-#include <cstdio>
+#include <cerrno>
 #include <chrono>
+#include <condition_variable>
+#include <cstdio>
 #include <cstring>
+#include <deque>
+#include <functional>
+#include <map>
+#include <memory>
 #include <mutex>
+#include <string>
 #include <thread>
 #include <vector>
 
@@ -47,6 +54,8 @@ using Clock = std::chrono::steady_clock;
 
 constexpr uint64_t kDefaultSlab = 256 * 1024;
 constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchange round
+constexpr uint64_t kDefaultSlotBytes = 256ull << 20;  // pinned bytes per slab when staging from files
+constexpr uint64_t kDefaultRingSlots = 4;            // slabs read ahead when staging from files
 
 // The local extraction copy of a load runs while the leaf hash is still going.
 // With fewer chains than about one consumer warp per SMSP the hash is bound by
@@ -74,6 +83,7 @@ struct DevBuf {
     cap = 0;
     const uint64_t want = std::max<uint64_t>(bytes, 256);
     if (cudaError_t e = cudaMalloc(&p, want); e != cudaSuccess) {
+      cudaGetLastError();  // reported here; keep it from later launch checks
       return set_errorf(TCX_RESOURCE_EXHAUSTED, "cudaMalloc(%llu) failed: %s",
                         static_cast<unsigned long long>(want), cuda_msg(e).c_str());
     }
@@ -87,6 +97,97 @@ struct DevBuf {
   }
   uint8_t* bytes() const { return static_cast<uint8_t*>(p); }
 };
+
+// One unit of host reading: fn(i) for i in [0, n), run by the reader pool's
+// threads; fn returns false (with code/err set under mu) on failure, after which
+// the remaining items are skipped.
+struct ReadBatch {
+  std::function<bool(uint64_t, ReadBatch&)> fn;
+  uint64_t n = 0;
+  std::atomic<uint64_t> done{0};
+  std::atomic<bool> failed{false};
+  uint64_t next = 0;  // next item to hand out (guarded by the pool's mutex)
+  std::mutex mu;
+  std::condition_variable cv;
+  tcx_status code = TCX_OK;
+  std::string err;
+  void fail(tcx_status c, const std::string& m) {
+    std::lock_guard<std::mutex> lk(mu);
+    if (code == TCX_OK) {
+      code = c;
+      err = m;
+    }
+    failed = true;
+  }
+};
+
+// Persistent host threads of a group that read file pieces into pinned slots.
+// Batches are served in submission order; a thread that finds every item of the
+// oldest batch handed out moves on to the next one, so several slabs are read
+// at once.
+class ReadPool {
+ public:
+  explicit ReadPool(int n) {
+    for (int i = 0; i < n; ++i) threads_.emplace_back([this] { work(); });
+  }
+  ~ReadPool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : threads_) t.join();
+  }
+  int size() const { return static_cast<int>(threads_.size()); }
+  void submit(const std::shared_ptr<ReadBatch>& b) {
+    if (b->n == 0) return;
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      q_.push_back(b);
+    }
+    cv_.notify_all();
+  }
+  // True once every item of b has run (or been skipped after a failure); false at the deadline.
+  static bool wait(ReadBatch& b, std::chrono::steady_clock::time_point deadline) {
+    std::unique_lock<std::mutex> lk(b.mu);
+    return b.cv.wait_until(lk, deadline, [&] { return b.done.load() == b.n; });
+  }
+
+ private:
+  void work() {
+    for (;;) {
+      std::shared_ptr<ReadBatch> b;
+      uint64_t i = 0;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return stop_ || !q_.empty(); });
+        if (q_.empty()) return;  // stop_ with nothing queued
+        b = q_.front();
+        i = b->next++;
+        if (b->next >= b->n) q_.pop_front();
+      }
+      if (!b->failed.load()) {
+        if (!b->fn(i, *b)) b->failed = true;
+      }
+      if (b->done.fetch_add(1) + 1 == b->n) {
+        std::lock_guard<std::mutex> lk(b->mu);
+        b->cv.notify_all();
+      }
+    }
+  }
+  std::mutex mu_;
+  std::condition_variable cv_;
+  std::deque<std::shared_ptr<ReadBatch>> q_;
+  std::vector<std::thread> threads_;
+  bool stop_ = false;
+};
+
+int affinity_cpus() {
+  cpu_set_t set;
+  CPU_ZERO(&set);
+  if (sched_getaffinity(0, sizeof set, &set) != 0) return 8;
+  return std::max(1, CPU_COUNT(&set));
+}
 
 }  // namespace
 
@@ -119,6 +220,12 @@ struct tcx_group {
   cudaEvent_t ev_push = nullptr;
   DevBuf ipc_records, barrier_word;
   uint8_t* h_ipc = nullptr;  // pinned, world records
+  // Streamed staging from files (tcx_group_load_files): a ring of pinned slots,
+  // kept between loads like the reference's pinned buffer pool, and the reader
+  // threads that fill them.
+  uint8_t* h_ring = nullptr;
+  uint64_t h_ring_bytes = 0;
+  std::unique_ptr<ReadPool> readers;
 };
 
 namespace {
@@ -392,6 +499,8 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   if (g->ev_push) cudaEventDestroy(g->ev_push);
   for (cudaStream_t s : g->s_peer)
     if (s) cudaStreamDestroy(s);
+  g->readers.reset();  // joins the reader threads before their ring goes away
+  if (g->h_ring) cudaFreeHost(g->h_ring);
   g->ipc_records.release();
   g->barrier_word.release();
   if (g->h_ipc) cudaFreeHost(g->h_ipc);
@@ -407,9 +516,168 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   return TCX_OK;
 }
 
-extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage,
-                                     void* d_view, const uint8_t* expected_root, tcx_load_result* out,
-                                     void* stream) {
+namespace {
+
+// One load's view of the files of the staged range, shared by the reader
+// threads (held by every batch of the load, so it outlives any piece in flight).
+struct FileStageCtx {
+  std::vector<tcx_file_segment> segs;  // sorted by dst_offset, non-overlapping; paths point into `paths`
+  std::vector<std::string> paths;
+  std::vector<int> fds;                 // per segment
+  std::vector<int> owned;               // distinct descriptors to close
+  ~FileStageCtx() {
+    for (int fd : owned) close(fd);
+  }
+};
+
+// Reads stage bytes [a, a + w) of the range into dst: file bytes where a segment
+// covers them, zero elsewhere (the canonical pads).
+bool read_stage_range(const FileStageCtx& c, uint64_t a, uint64_t w, uint8_t* dst, ReadBatch& b) {
+  const auto& sg = c.segs;
+  size_t k = std::partition_point(sg.begin(), sg.end(),
+                                  [&](const tcx_file_segment& x) { return x.dst_offset + x.length <= a; }) -
+             sg.begin();
+  uint64_t pos = a;
+  const uint64_t end = a + w;
+  while (pos < end) {
+    if (k >= sg.size() || sg[k].dst_offset >= end) {
+      std::memset(dst + (pos - a), 0, end - pos);
+      break;
+    }
+    const tcx_file_segment& x = sg[k];
+    if (x.dst_offset > pos) {
+      std::memset(dst + (pos - a), 0, x.dst_offset - pos);
+      pos = x.dst_offset;
+    }
+    const uint64_t e = std::min(end, x.dst_offset + x.length);
+    uint64_t got = 0;
+    const uint64_t want = e - pos, foff = x.file_offset + (pos - x.dst_offset);
+    while (got < want) {
+      const ssize_t r = pread(c.fds[k], dst + (pos - a) + got, want - got, static_cast<off_t>(foff + got));
+      if (r < 0 && errno == EINTR) continue;
+      if (r <= 0) {
+        char msg[512];
+        snprintf(msg, sizeof msg, "short read while staging %s at offset %llu (%llu of %llu bytes)", x.path,
+                 static_cast<unsigned long long>(foff + got), static_cast<unsigned long long>(got),
+                 static_cast<unsigned long long>(want));
+        b.fail(TCX_DATA_LOSS, msg);
+        return false;
+      }
+      got += static_cast<uint64_t>(r);
+    }
+    pos = e;
+    ++k;
+  }
+  return true;
+}
+
+// Streams this rank's staged range from files: reader threads pread slab j into
+// pinned slot j % K (row r of the slot = leaf r's piece of the slab), and as soon
+// as a slot is full its H2D and hash pass are queued; slot reuse waits for the
+// H2D of the slab that last used it. Reads of up to K slabs run ahead.
+template <class Enqueue>
+tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t mine, uint64_t L, uint64_t S, uint64_t J,
+                            uint64_t n_full, uint64_t tail, Enqueue&& enqueue_slab, Clock::time_point deadline) {
+  if (fs.n_segments > 0 && fs.segments == nullptr) return set_error(TCX_INVALID_ARGUMENT, "segments is null");
+  auto ctx = std::make_shared<FileStageCtx>();
+  ctx->segs.reserve(fs.n_segments);
+  ctx->paths.reserve(fs.n_segments);
+  for (uint64_t i = 0; i < fs.n_segments; ++i) {
+    const tcx_file_segment& x = fs.segments[i];
+    if (x.path == nullptr) return set_errorf(TCX_INVALID_ARGUMENT, "segment %llu has no path", static_cast<unsigned long long>(i));
+    if (x.length == 0) continue;
+    if (x.dst_offset > mine || x.length > mine - x.dst_offset)
+      return set_errorf(TCX_INVALID_ARGUMENT, "segment %llu lies outside the staged range of %llu bytes",
+                        static_cast<unsigned long long>(i), static_cast<unsigned long long>(mine));
+    ctx->paths.emplace_back(x.path);
+    ctx->segs.push_back(x);
+  }
+  for (size_t i = 0; i < ctx->segs.size(); ++i) ctx->segs[i].path = ctx->paths[i].c_str();
+  std::sort(ctx->segs.begin(), ctx->segs.end(),
+            [](const tcx_file_segment& x, const tcx_file_segment& y) { return x.dst_offset < y.dst_offset; });
+  for (size_t i = 1; i < ctx->segs.size(); ++i)
+    if (ctx->segs[i].dst_offset < ctx->segs[i - 1].dst_offset + ctx->segs[i - 1].length)
+      return set_error(TCX_INVALID_ARGUMENT, "segments overlap in the staged range");
+  std::map<std::string, int> opened;
+  ctx->fds.resize(ctx->segs.size());
+  for (size_t i = 0; i < ctx->segs.size(); ++i) {
+    auto it = opened.find(ctx->segs[i].path);
+    if (it == opened.end()) {
+      const int fd = open(ctx->segs[i].path, O_RDONLY | O_CLOEXEC);
+      if (fd < 0) return set_errorf(TCX_NOT_FOUND, "open failed: %s", ctx->segs[i].path);
+      ctx->owned.push_back(fd);
+      it = opened.emplace(ctx->segs[i].path, fd).first;
+    }
+    ctx->fds[i] = it->second;
+  }
+
+  const uint64_t n_rows = n_full + (tail > 0 ? 1 : 0);
+  const uint64_t slot = n_rows * S;
+  const uint64_t K = std::min<uint64_t>(J, fs.ring_slots > 0 ? static_cast<uint64_t>(fs.ring_slots) : kDefaultRingSlots);
+  if (g->h_ring_bytes < K * slot) {
+    if (g->h_ring) cudaFreeHost(g->h_ring);
+    g->h_ring = nullptr;
+    g->h_ring_bytes = 0;
+    if (cudaError_t e = cudaHostAlloc(&g->h_ring, K * slot, cudaHostAllocPortable); e != cudaSuccess) {
+      cudaGetLastError();
+      return set_errorf(TCX_RESOURCE_EXHAUSTED, "pinned staging ring of %llu bytes: %s",
+                        static_cast<unsigned long long>(K * slot), cuda_msg(e).c_str());
+    }
+    g->h_ring_bytes = K * slot;
+  }
+  const int nt = fs.read_threads > 0 ? fs.read_threads : std::min(32, affinity_cpus());
+  if (!g->readers || g->readers->size() != nt) {
+    g->readers.reset();
+    g->readers = std::make_unique<ReadPool>(nt);
+  }
+
+  std::vector<std::shared_ptr<ReadBatch>> batches(J);
+  uint64_t dispatched = 0;
+  tcx_status st = TCX_OK;
+  for (uint64_t j = 0; j < J && st == TCX_OK; ++j) {
+    while (dispatched < J && dispatched < j + K) {
+      if (dispatched >= K && (st = wait_event(g, g->slab_events[dispatched - K], deadline)) != TCX_OK) break;
+      auto b = std::make_shared<ReadBatch>();
+      const uint64_t jj = dispatched, off = jj * S;
+      uint8_t* dst = g->h_ring + (jj % K) * slot;
+      b->n = n_rows;
+      b->fn = [ctx, jj, off, dst, S, L, n_full, tail](uint64_t r, ReadBatch& bb) {
+        (void)jj;
+        if (r < n_full) return read_stage_range(*ctx, r * L + off, std::min(S, L - off), dst + r * S, bb);
+        if (tail <= off) return true;
+        return read_stage_range(*ctx, n_full * L + off, std::min(S, tail - off), dst + r * S, bb);
+      };
+      batches[jj] = b;
+      g->readers->submit(b);
+      ++dispatched;
+    }
+    if (st != TCX_OK) break;
+    if (!ReadPool::wait(*batches[j], deadline)) {
+      st = set_error(TCX_DEADLINE_EXCEEDED, "reading the staged range from files timed out");
+      break;
+    }
+    if (batches[j]->failed) {
+      std::lock_guard<std::mutex> lk(batches[j]->mu);
+      st = set_error(batches[j]->code != TCX_OK ? batches[j]->code : TCX_INTERNAL, batches[j]->err);
+      break;
+    }
+    uint8_t* src = g->h_ring + (j % K) * slot;
+    st = enqueue_slab(j, src, S, src + n_full * S);
+  }
+  if (st != TCX_OK) {
+    // Nothing of this load may still write into the ring once the call returns:
+    // skip what is not started and wait for reads in progress and queued copies.
+    for (uint64_t k = 0; k < dispatched; ++k) batches[k]->failed = true;
+    for (uint64_t k = 0; k < dispatched; ++k)
+      ReadPool::wait(*batches[k], Clock::now() + std::chrono::milliseconds(g->timeout_ms));
+    cudaStreamSynchronize(g->s_copy);
+    cudaGetLastError();
+  }
+  return st;
+}
+
+tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, const tcx_file_stage* files,
+                      void* d_stage, void* d_view, const uint8_t* expected_root, tcx_load_result* out, void* stream) {
   if (g == nullptr) return set_error(TCX_INVALID_ARGUMENT, "group is null");
   std::lock_guard<std::mutex> lock(g->mu);
   if (g->world > 1 && g->comm == nullptr)
@@ -697,29 +965,52 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_hash, g->ev_start, 0));
   TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->ev_start, 0));
   uint64_t h2d_bytes = 0;
+  float read_ms = 0.f;
   if (mine > 0) {
-    if (hstage != nullptr) {
-      uint64_t S = plan->slab_bytes ? plan->slab_bytes : kDefaultSlab;
-      S = std::max<uint64_t>(64, S - S % 64);
+    if (hstage != nullptr || files != nullptr) {
+      // Slabs: slab j is bytes [j*S, (j+1)*S) of every leaf of the range (one 2-D
+      // copy: n_full rows at pitch L, plus the short last leaf), so every leaf's
+      // chain advances as each slab lands.
       const uint64_t n_full = mine / L, tail = mine - n_full * L;
       const uint64_t span = n_full > 0 ? L : tail;  // bytes per leaf to cover
+      const uint64_t n_rows = n_full + (tail > 0 ? 1 : 0);
+      uint64_t S = plan->slab_bytes;
+      if (S == 0 && files != nullptr) {
+        // From files, a slab is one pinned slot: about slot_bytes per slab.
+        // S is a power of two from 64 bytes up to the leaf.
+        const uint64_t want = files->slot_bytes ? files->slot_bytes : kDefaultSlotBytes;
+        S = 64;
+        while (S * 2 <= span && S * 2 * n_rows <= want) S *= 2;
+      }
+      if (S == 0) S = kDefaultSlab;
+      S = std::max<uint64_t>(64, S - S % 64);
       const uint64_t J = (span + S - 1) / S;
       if ((st = ensure_events(g->slab_events, J)) != TCX_OK) return st;
-      for (uint64_t j = 0; j < J; ++j) {
+      // H2D of slab j from src (rows at src_pitch; the short leaf's piece at tsrc),
+      // then the streamed hash pass over it.
+      auto enqueue_slab = [&](uint64_t j, const uint8_t* src, uint64_t src_pitch, const uint8_t* tsrc) -> tcx_status {
         const uint64_t off = j * S;
         if (n_full > 0 && off < L) {
           const uint64_t w = std::min(S, L - off);
-          TCX_CUDA_TRY(cudaMemcpy2DAsync(stage + off, L, hstage + off, L, w, n_full, cudaMemcpyHostToDevice, g->s_copy));
+          TCX_CUDA_TRY(cudaMemcpy2DAsync(stage + off, L, src, src_pitch, w, n_full, cudaMemcpyHostToDevice, g->s_copy));
         }
         if (tail > off) {
           const uint64_t w = std::min(S, tail - off);
-          TCX_CUDA_TRY(cudaMemcpyAsync(stage + n_full * L + off, hstage + n_full * L + off, w, cudaMemcpyHostToDevice,
-                                       g->s_copy));
+          TCX_CUDA_TRY(cudaMemcpyAsync(stage + n_full * L + off, tsrc, w, cudaMemcpyHostToDevice, g->s_copy));
         }
         TCX_CUDA_TRY(cudaEventRecord(g->slab_events[j], g->s_copy));
         TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_hash, g->slab_events[j], 0));
-        st = launch_leaf_pass(stage, mine, L, static_cast<uint32_t>(n_mine), off, S,
-                              static_cast<uint32_t*>(g->states.p), g->digests_mine.p, g->s_hash);
+        return launch_leaf_pass(stage, mine, L, static_cast<uint32_t>(n_mine), off, S,
+                                static_cast<uint32_t*>(g->states.p), g->digests_mine.p, g->s_hash);
+      };
+      if (files == nullptr) {
+        for (uint64_t j = 0; j < J; ++j) {
+          if ((st = enqueue_slab(j, hstage + j * S, L, hstage + n_full * L + j * S)) != TCX_OK) return st;
+        }
+      } else {
+        const auto t_read = Clock::now();
+        st = stage_from_files(g, *files, mine, L, S, J, n_full, tail, enqueue_slab, deadline);
+        read_ms = std::chrono::duration<float, std::milli>(Clock::now() - t_read).count();
         if (st != TCX_OK) return st;
       }
       h2d_bytes = mine;
@@ -889,6 +1180,7 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   out->hash_ms = elapsed_ms(g->ev_start, g->ev_hash);
   out->exchange_ms = elapsed_ms(g->ev_h2d, g->ev_exch);
   out->total_ms = elapsed_ms(g->ev_start, g->ev_end);
+  out->stage_read_ms = read_ms;
   if (view_hash) {
     encode_multihash(g->h_root + 64, out->view_multihash);
     out->view_leaf_bytes = view_leaf;
@@ -896,6 +1188,21 @@ extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, co
   if (expected_root != nullptr && std::memcmp(expected_root, out->root, 32) != 0)
     return set_error(TCX_DATA_LOSS, "ARTIFACT_ID_MISMATCH: data multihash of the loaded bytes differs from the expected one");
   return TCX_OK;
+}
+
+}  // namespace
+
+extern "C" tcx_status tcx_group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_stage, void* d_stage,
+                                     void* d_view, const uint8_t* expected_root, tcx_load_result* out,
+                                     void* stream) {
+  return group_load(g, plan, h_stage, nullptr, d_stage, d_view, expected_root, out, stream);
+}
+
+extern "C" tcx_status tcx_group_load_files(tcx_group* g, const tcx_load_plan* plan, const tcx_file_stage* files,
+                                           void* d_stage, void* d_view, const uint8_t* expected_root,
+                                           tcx_load_result* out, void* stream) {
+  if (files == nullptr) return set_error(TCX_INVALID_ARGUMENT, "files is null");
+  return group_load(g, plan, nullptr, files, d_stage, d_view, expected_root, out, stream);
 }
 
 namespace {

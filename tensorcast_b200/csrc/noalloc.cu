@@ -37,6 +37,20 @@ constexpr uint64_t kScratchBytes = kRootOffset + 256;
 // cudaGetSymbolAddress, once per device, below.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kScratchBytes];
 
+// Puts the calling thread's current device back when the call returns.
+struct DeviceRestore {
+  int prior = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&prior) != cudaSuccess) {
+      cudaGetLastError();
+      prior = -1;
+    }
+  }
+  ~DeviceRestore() {
+    if (prior >= 0) cudaSetDevice(prior);
+  }
+};
+
 struct NoAllocDevice {
   std::mutex mu;     // serialises calls on one device (the scratch is shared)
   uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
@@ -77,9 +91,24 @@ extern "C" tcx_status tcx_multihash_from_gpu_noalloc(const void* d_src, uint64_t
                       static_cast<unsigned long long>(kNoAllocMaxLeaves));
   if (device_id < 0 || device_id >= kMaxDevices)
     return set_errorf(TCX_INTERNAL, "Failed to set CUDA device %d: invalid device ordinal", device_id);
-  if (cudaError_t e = cudaSetDevice(device_id); e != cudaSuccess)
+  // The caller's current device is restored on every return: this entry point
+  // serves engines that drive devices from their own threads.
+  DeviceRestore restore;
+  if (cudaError_t e = cudaSetDevice(device_id); e != cudaSuccess) {
+    cudaGetLastError();
     return set_errorf(TCX_INTERNAL, "Failed to set CUDA device %d: %s", device_id, cuda_msg(e).c_str());
-
+  }
+  const auto s = static_cast<cudaStream_t>(stream);
+  if (s != nullptr) {
+    int stream_dev = -1;
+    if (cudaError_t e = cudaStreamGetDevice(s, &stream_dev); e != cudaSuccess) {
+      cudaGetLastError();
+      return set_errorf(TCX_INVALID_ARGUMENT, "cannot query the stream's device: %s", cuda_msg(e).c_str());
+    }
+    if (stream_dev != device_id)
+      return set_errorf(TCX_INVALID_ARGUMENT, "stream belongs to device %d, not to device_id %d", stream_dev,
+                        device_id);
+  }
   NoAllocDevice& dev = g_devices[device_id];
   std::lock_guard<std::mutex> lock(dev.mu);
   if (dev.scratch == nullptr) {
@@ -90,6 +119,12 @@ extern "C" tcx_status tcx_multihash_from_gpu_noalloc(const void* d_src, uint64_t
     if (e != cudaSuccess || p == nullptr)
       return set_error(TCX_INTERNAL, "GPU hashing unavailable; CPU fallback disabled: cudaGetSymbolAddress failed: " +
                                          cuda_msg(e));
+    // Every kernel this entry point may launch is loaded now, so that no later
+    // call, whatever its shape, needs device memory for a module load.
+    if (tcx_status pst = preload_hash_kernels(); pst != TCX_OK) {
+      const std::string msg = tcx_last_error();
+      return set_error(pst, "GPU hashing unavailable; CPU fallback disabled: " + msg);
+    }
     dev.scratch = static_cast<uint8_t*>(p);
   }
   // Nothing in the scratch has to start at zero: the leaf kernel writes every
@@ -97,7 +132,6 @@ extern "C" tcx_status tcx_multihash_from_gpu_noalloc(const void* d_src, uint64_t
   uint8_t* digests = dev.scratch;
   uint8_t* merkle = dev.scratch + kDigestBytes;
   uint8_t* d_root = dev.scratch + kRootOffset;
-  const auto s = static_cast<cudaStream_t>(stream);
   st = launch_leaf_pass(d_src, total_bytes, leaf, static_cast<uint32_t>(n), 0, ~0ull, nullptr, digests, s);
   if (st == TCX_OK) st = launch_merkle(digests, n, merkle, d_root, s);
   uint8_t root[32];

@@ -33,6 +33,7 @@ tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, ui
                             uint64_t seg_len, uint32_t* states, void* d_digests, cudaStream_t stream);
 tcx_status launch_merkle(const uint8_t* digests, uint64_t n, uint8_t* scratch, uint8_t* root, cudaStream_t stream);
 uint64_t merkle_scratch_bytes(uint64_t n);
+tcx_status preload_hash_kernels();
 void encode_multihash(const uint8_t digest[32], char out[57]);
 
 inline std::string cuda_msg(cudaError_t e) {
@@ -41,11 +42,15 @@ inline std::string cuda_msg(cudaError_t e) {
 
 }  // namespace tcx
 
-// Returns TCX_INTERNAL with a message naming the failing call.
+// Returns TCX_INTERNAL with a message naming the failing call. The runtime's
+// per-thread last error is reset (it is reported here), so that a later launch
+// check on this thread does not pick up an error of this call, such as a failed
+// allocation.
 #define TCX_CUDA_TRY(call)                                                                         \
   do {                                                                                             \
     cudaError_t tcx_e_ = (call);                                                                   \
     if (tcx_e_ != cudaSuccess) {                                                                   \
+      cudaGetLastError();                                                                          \
       return ::tcx::set_error(TCX_INTERNAL, std::string(#call " failed: ") + ::tcx::cuda_msg(tcx_e_)); \
     }                                                                                              \
   } while (0)

@@ -166,10 +166,17 @@ class Group:
             dist.broadcast_object_list(obj, src=0)
         return cls(world, rank, device, obj[0] if world > 1 else None, timeout_ms)
 
-    def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, permutes=(), view_bytes=None,
-             expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0,
-             view_hash: bool = False, peer_push: bool = False, target_ranges=None, all_gather: bool = False) -> dict:
-        """Runs one load; returns the result fields as a dict. h_stage None: device-resident.
+    def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, files=None, permutes=(),
+             view_bytes=None, expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0,
+             view_hash: bool = False, peer_push: bool = False, target_ranges=None, all_gather: bool = False,
+             read_threads: int = 0, ring_slots: int = 0, slot_bytes: int = 0) -> dict:
+        """Runs one load; returns the result fields as a dict. h_stage None and files None:
+        device-resident (d_stage already holds this rank's range).
+
+        files: this rank's staged range as (path, file_offset, stage_offset, length) segments
+        (stage offsets relative to bounds[rank]; uncovered bytes are zero): the range is read
+        inside the call by the group's reader threads into a ring of pinned slots, overlapped
+        with the copies to the device and the hash (tcx_group_load_files).
 
         peer_push: exchange by copying into the peers' views over NVLink (d_view must be a
         cudaMalloc allocation of this process, e.g. a torch CUDA tensor); all_gather: a windowed
@@ -191,13 +198,27 @@ class Group:
             exp = ctypes.create_string_buffer(bytes(expected_root), 32)
         ptr = lambda x: None if x is None else (x.data_ptr() if hasattr(x, "data_ptr") else int(x))  # noqa: E731
         stream = torch.cuda.current_stream().cuda_stream
-        _native.call("tcx_group_load", self._h, ctypes.byref(plan.c), ptr(h_stage), ptr(d_stage), ptr(d_view), exp,
-                     ctypes.byref(res), stream)
+        if files is not None:
+            if h_stage is not None:
+                raise ValueError("give either h_stage or files")
+            segs = (_native.FileSegment * max(len(files), 1))()
+            keep = []
+            for i, (path, foff, doff, ln) in enumerate(files):
+                p = os.fsencode(path)
+                keep.append(p)
+                segs[i] = _native.FileSegment(p, int(foff), int(doff), int(ln))
+            fs = _native.FileStage(segs, len(files), int(read_threads), int(ring_slots), int(slot_bytes))
+            _native.call("tcx_group_load_files", self._h, ctypes.byref(plan.c), ctypes.byref(fs), ptr(d_stage),
+                         ptr(d_view), exp, ctypes.byref(res), stream)
+        else:
+            _native.call("tcx_group_load", self._h, ctypes.byref(plan.c), ptr(h_stage), ptr(d_stage), ptr(d_view),
+                         exp, ctypes.byref(res), stream)
         return {"root": bytes(res.root), "multihash": res.multihash.decode(), "leaves": res.leaves,
                 "h2d_bytes": res.h2d_bytes, "peer_send_bytes": res.peer_send_bytes,
                 "peer_recv_bytes": res.peer_recv_bytes, "h2d_ms": res.h2d_ms, "hash_ms": res.hash_ms,
                 "exchange_ms": res.exchange_ms, "total_ms": res.total_ms,
-                "view_multihash": res.view_multihash.decode(), "view_leaf_bytes": res.view_leaf_bytes}
+                "view_multihash": res.view_multihash.decode(), "view_leaf_bytes": res.view_leaf_bytes,
+                "stage_read_ms": res.stage_read_ms}
 
     def close(self) -> None:
         if self._h:

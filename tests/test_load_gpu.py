@@ -236,3 +236,89 @@ def test_reference_replicated_case_into_target(cuda_device):
         assert (target.cpu().numpy() == payload).all()
     finally:
         g.close()
+
+
+def _write_shuffled_files(tmp_path, canon, meta, n_files=2, seed=0):
+    """Writes every tensor's bytes into one of n_files files, in a shuffled payload order with
+    junk between them; returns (path, file_offset, canonical_offset, length) per tensor."""
+    rng = np.random.default_rng(seed)
+    names = list(meta)
+    order = [names[i] for i in rng.permutation(len(names))]
+    bufs = [bytearray(int(rng.integers(0, 64))) for _ in range(n_files)]
+    out = []
+    for k, n in enumerate(order):
+        off, shape, es = meta[n]
+        ln = (int(np.prod(shape)) if shape else 1) * es
+        f = k % n_files
+        bufs[f] += bytes(int(rng.integers(0, 24)))  # junk before the tensor
+        out.append((str(tmp_path / f"part{f}.bin"), len(bufs[f]), off, ln))
+        bufs[f] += canon[off:off + ln].tobytes()
+    for f in range(n_files):
+        (tmp_path / f"part{f}.bin").write_bytes(bytes(bufs[f]) + bytes(100))
+    return out
+
+
+def _segments_for(tensor_segs, lo, hi):
+    segs = []
+    for path, foff, coff, ln in tensor_segs:
+        a, b = max(lo, coff), min(hi, coff + ln)
+        if a < b:
+            segs.append((path, foff + (a - coff), a - lo, b - a))
+    return segs
+
+
+@pytest.mark.parametrize("threads,slot_bytes", [(1, 0), (4, 1 << 16), (7, 3 << 12)])
+def test_file_staged_load_matches_oracle(cuda_device, tmp_path, threads, slot_bytes):
+    """tcx_group_load_files: the range read from several files (shuffled payload order, pads
+    between tensors left to the loader), slabs smaller than the ring so slots are reused;
+    root and view bit-exact against the oracles."""
+    g = Group(1, 0, 0)
+    try:
+        for seed in range(4):
+            canon, meta = oviews.canonical_bytes(random_tensors(seed + 100, n=24))
+            index = index_from_meta(meta, canon.size)
+            tseg = _write_shuffled_files(tmp_path, canon, meta, n_files=1 + seed % 3, seed=seed)
+            rng = np.random.default_rng(seed)
+            slices, transpose, subset, spec = random_view(meta, rng)
+            plan = plan_view(index, spec, subset)
+            for leaf in (64, 1024, 4096 + 64):
+                d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+                d_view = torch.zeros(max(plan.view_bytes, 1), dtype=torch.uint8, device="cuda")
+                res = g.load(canon.size, leaf, [0, canon.size], [plan.jobs], d_stage=d_stage, d_view=d_view,
+                             files=_segments_for(tseg, 0, canon.size), permutes=plan.permutes,
+                             view_bytes=plan.view_bytes, read_threads=threads, ring_slots=2,
+                             slot_bytes=slot_bytes)
+                assert res["root"] == oracle.tree_root(oracle.leaf_digests(canon, leaf))
+                assert (d_stage.cpu().numpy() == canon).all()
+                want = oviews.materialize_view(canon, meta, slices, transpose, subset)
+                assert (d_view.cpu().numpy()[: plan.view_bytes] == want).all()
+    finally:
+        g.close()
+
+
+def test_file_staged_load_errors_then_recovers(cuda_device, tmp_path):
+    canon = np.random.default_rng(5).integers(0, 256, size=(3 << 20) + 4000, dtype=np.uint8)
+    path = tmp_path / "a.bin"
+    path.write_bytes(canon.tobytes())
+    leaf = 1 << 18
+    g = Group(1, 0, 0)
+    try:
+        d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+        kw = dict(d_stage=d_stage, d_view=d_stage, view_bytes=canon.size, read_threads=3, ring_slots=2,
+                  slot_bytes=1 << 16)
+        with pytest.raises(_native.TcxError) as e:
+            g.load(canon.size, leaf, [0, canon.size], [np.zeros(0, JOB_DTYPE)],
+                   files=[(str(tmp_path / "missing.bin"), 0, 0, canon.size)], **kw)
+        assert e.value.code == _native.NOT_FOUND
+        short = tmp_path / "short.bin"
+        short.write_bytes(canon[: canon.size - 100].tobytes())
+        with pytest.raises(_native.TcxError) as e:
+            g.load(canon.size, leaf, [0, canon.size], [np.zeros(0, JOB_DTYPE)],
+                   files=[(str(short), 0, 0, canon.size)], **kw)
+        assert e.value.code == _native.DATA_LOSS and "short read" in e.value.message
+        res = g.load(canon.size, leaf, [0, canon.size], [np.zeros(0, JOB_DTYPE)],
+                     files=[(str(path), 0, 0, canon.size)], **kw)
+        assert res["root"] == oracle.tree_root(oracle.leaf_digests(canon, leaf))
+        assert res["stage_read_ms"] > 0
+    finally:
+        g.close()
