@@ -439,8 +439,14 @@ def main() -> None:
     # timed step (tcx_group_load_files). Reader threads: the CPUs this rank may use,
     # shared evenly by the ranks of this host.
     files_mine = canonical_segments(index, lo, hi)
-    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
-    read_threads = max(2, min(32, len(os.sched_getaffinity(0)) // max(1, local_world)))
+    affinity = tuple(sorted(os.sched_getaffinity(0)))
+    sharing = 1
+    if world > 1:
+        import socket
+        everyone = [None] * world
+        dist.all_gather_object(everyone, (socket.gethostname(), affinity))
+        sharing = sum(1 for x in everyone if x == (socket.gethostname(), affinity))
+    read_threads = max(2, min(32, len(affinity) // sharing))
     # Staged bytes in page-locked host memory as well (setup), for the from-pinned-memory
     # form of e2e and the host-to-device bound: the file's own tmpfs pages mapped and
     # registered in place when asked, else a pinned copy assembled with parallel preads.

@@ -288,7 +288,8 @@ typedef struct tcx_load_plan {
  * send/recv: every rank maps every peer's view (CUDA IPC; d_view must be memory
  * this process allocated with cudaMalloc) and copies the peers' view pieces
  * from its staged bytes directly into those views over NVLink with the copy
- * engines (one 2-D copy per piece, one stream per peer), so extraction and
+ * engines (one 2-D copy per piece, one stream per peer; a peer that is a thread
+ * of this process is written through its own pointer), so extraction and
  * transfer are one pass with no pack or receive buffers and no SM time is taken
  * from the leaf hash running at the same time. NCCL carries only the handle
  * exchange and two one-word barriers. */
@@ -427,6 +428,20 @@ tcx_status tcx_group_unique_id(uint8_t* out128);
 tcx_status tcx_group_create(const uint8_t* unique_id, int world, int rank, int device, int64_t timeout_ms,
                             tcx_group** out);
 
+/* tcx_group_create for rank threads of one process, the reference daemon's model
+ * (try_collective_disk_load called by N rank threads that rendezvous on group_id,
+ * collective_disk_loader.cc:8159-8277; clique over the local GPUs, :229-247):
+ * the first thread to join `group_id` creates the NCCL unique id and every rank
+ * thread of the group takes it from an in-process table, then joins as
+ * tcx_group_create does (one communicator per thread, waiting at most timeout_ms
+ * for the others). A rank joining twice, or a different world size under the same
+ * id, is INVALID_ARGUMENT; an id whose ranks did not all join within timeout_ms
+ * starts a new generation at its next join. Loads of such groups may use
+ * TCX_LOAD_PEER_PUSH: peers in the same process are written through their own
+ * pointers (peer access enabled), peers in other processes through CUDA IPC. */
+tcx_status tcx_group_join(const char* group_id, int world, int rank, int device, int64_t timeout_ms,
+                          tcx_group** out);
+
 /* Releases the group's communicator, streams and device buffers. */
 tcx_status tcx_group_destroy(tcx_group* g);
 
@@ -462,7 +477,7 @@ typedef struct tcx_file_stage {
   uint64_t n_segments;
   int read_threads;                 /* host reader threads (0: the CPUs the caller may run on, <= 32) */
   int ring_slots;                   /* pinned slabs read ahead (0: 4) */
-  uint64_t slot_bytes;              /* pinned bytes per slab when plan->slab_bytes is 0 (0: 256 MiB) */
+  uint64_t slot_bytes;              /* pinned bytes per slab when plan->slab_bytes is 0 (0: 512 MiB) */
 } tcx_file_stage;
 
 /* tcx_group_load with the staged range read from files inside the call: the

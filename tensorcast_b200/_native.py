@@ -143,6 +143,7 @@ _SIGNATURES = {
     "tcx_bind_device_cpus": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_int)]),
     "tcx_group_unique_id": (_c.c_int, [_c.c_void_p]),
     "tcx_group_create": (_c.c_int, [_c.c_void_p, _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.POINTER(_c.c_void_p)]),
+    "tcx_group_join": (_c.c_int, [_c.c_char_p, _c.c_int, _c.c_int, _c.c_int, _c.c_int64, _c.POINTER(_c.c_void_p)]),
     "tcx_group_destroy": (_c.c_int, [_c.c_void_p]),
     "tcx_group_load": (_c.c_int, [_c.c_void_p, _c.POINTER(LoadPlan), _c.c_void_p, _c.c_void_p, _c.c_void_p,
                                   _c.c_void_p, _c.POINTER(LoadResult), _c.c_void_p]),

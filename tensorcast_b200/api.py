@@ -14,9 +14,11 @@ Same names, arguments and error behaviour as the TensorCast SDK for this path:
   (tensorcast/api/context.py:13-18)
 
 Instead of a gRPC call into a daemon, ``tensor_dict`` runs the load in-process: each
-rank (one process per GPU, ranks joined by torch.distributed) stages its leaf-aligned
-1/N of the canonical bytes, the ranks exchange the bytes of each other's views over
-NVLink, and every rank returns its tensors as views of one device buffer.
+rank stages its leaf-aligned 1/N of the canonical bytes (read from the files inside the
+load), the ranks exchange the bytes of each other's views over NVLink, and every rank
+returns its tensors as views of one device buffer. Ranks are either one process per GPU
+joined by torch.distributed, or -- the reference daemon's model -- threads of one
+process that call with the same ``CollectiveLoadGroup.group_id`` (one thread per GPU).
 
 Verification follows verification_stage.cc:55-141: the data multihash of the loaded
 bytes is always computed on the GPU (leaf size from the adaptive policy of
@@ -28,6 +30,8 @@ from __future__ import annotations
 
 import json
 import os
+import threading
+import time
 from dataclasses import dataclass
 
 import numpy as np
@@ -78,29 +82,90 @@ class GetArtifactOptions:
 _GROUPS: dict = {}
 
 
+def _process_model(world: int, rank: int) -> bool:
+    """True when torch.distributed holds this group's ranks (one process per GPU);
+    otherwise the ranks are threads of this process that find each other by group id
+    (the reference daemon's model)."""
+    import torch.distributed as dist
+    return dist.is_available() and dist.is_initialized() and dist.get_world_size() == world and \
+        dist.get_rank() == rank
+
+
+_GROUPS_LOCK = threading.Lock()
+
+
 def _group_for(device_index: int, world: int, rank: int, group_id: str) -> Group:
     key = (device_index, world, rank, group_id)
-    g = _GROUPS.get(key)
+    with _GROUPS_LOCK:
+        g = _GROUPS.get(key)
     if g is None:
         if world == 1:
             g = Group(1, 0, device_index)
-        else:
-            import torch.distributed as dist
-            if not dist.is_initialized() or dist.get_world_size() != world or dist.get_rank() != rank:
-                raise ArtifactError("collective load needs torch.distributed initialised with the group's ranks",
-                                    "FAILED_PRECONDITION")
+        elif _process_model(world, rank):
             g = Group.from_torch_distributed(device_index)
-        _GROUPS[key] = g
+        elif group_id:
+            g = Group.join(group_id, world, rank, device_index)
+        else:
+            raise ArtifactError("a collective load needs torch.distributed initialised with the group's ranks, or a "
+                                "group_id shared by the rank threads of this process", "FAILED_PRECONDITION")
+        with _GROUPS_LOCK:
+            _GROUPS[key] = g
     return g
 
 
-def gather_rank_jobs(jobs: np.ndarray, world: int) -> list:
-    """Every rank's view copy jobs (all ranks call it; one all_gather of the job bytes)."""
+_RDV = threading.Condition()
+_RDV_TABLE: dict = {}
+
+
+def _gather_in_process(group_id: str, world: int, rank: int, payload: bytes, timeout_s: float = 120.0) -> list:
+    """All-gather of one bytes object per rank among the rank threads of this process
+    that share group_id; repeated calls with the same id form successive rounds."""
+    deadline = time.monotonic() + timeout_s
+    with _RDV:
+        while True:
+            e = _RDV_TABLE.get(group_id)
+            if e is None:
+                e = _RDV_TABLE[group_id] = {"world": world, "items": [None] * world, "n": 0, "taken": 0}
+            if e["world"] != world:
+                raise ArtifactError(f"group {group_id} gathered with world sizes {e['world']} and {world}",
+                                    "INVALID_ARGUMENT")
+            if e["items"][rank] is None:
+                break
+            if not _RDV.wait(deadline - time.monotonic()):  # an earlier round still being read
+                raise ArtifactError(f"group {group_id}: rank {rank} timed out waiting for the previous round",
+                                    "DEADLINE_EXCEEDED")
+        e["items"][rank] = payload
+        e["n"] += 1
+        _RDV.notify_all()
+        while e["n"] < world:
+            if not _RDV.wait(deadline - time.monotonic()) and e["n"] < world:
+                # withdraw this rank's item so that a later round starts clean
+                e["items"][rank] = None
+                e["n"] -= 1
+                if e["n"] == 0:
+                    del _RDV_TABLE[group_id]
+                _RDV.notify_all()
+                raise ArtifactError(f"group {group_id}: rank {rank} timed out waiting for {world - e['n'] - 1} "
+                                    "rank(s)", "DEADLINE_EXCEEDED")
+        out = list(e["items"])
+        e["taken"] += 1
+        if e["taken"] == world:
+            del _RDV_TABLE[group_id]
+            _RDV.notify_all()
+    return out
+
+
+def gather_rank_jobs(jobs: np.ndarray, world: int, rank: int | None = None, group_id: str | None = None) -> list:
+    """Every rank's view copy jobs (all ranks call it): one all_gather of the job bytes
+    over torch.distributed, or, for rank threads of one process, through group_id."""
     if world == 1:
         return [jobs]
-    import torch.distributed as dist
-    out = [None] * world
-    dist.all_gather_object(out, jobs.tobytes())
+    if rank is None or _process_model(world, rank):
+        import torch.distributed as dist
+        out = [None] * world
+        dist.all_gather_object(out, jobs.tobytes())
+    else:
+        out = _gather_in_process(group_id, world, rank, jobs.tobytes())
     return [np.frombuffer(b, dtype=JOB_DTYPE).copy() for b in out]
 
 
@@ -168,7 +233,7 @@ class Artifact:
         (hash + exchange + view) into d_view (None: the staged buffer, for an identity view)."""
         T = self.index.total_bytes
         L = self.leaf_chunk_bytes or determine_leaf_chunk_size(T, DEFAULT_LEAF_CHUNK_BYTES)
-        rank_jobs = gather_rank_jobs(jobs, world)
+        rank_jobs = gather_rank_jobs(jobs, world, rank, coll.group_id if coll else None)
         bounds = stage_bounds(T, L, world)
         lo, hi = bounds[rank], bounds[rank + 1]
         with torch.cuda.device(dev_index):

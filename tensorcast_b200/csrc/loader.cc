@@ -36,6 +36,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <random>
 #include <string>
 #include <thread>
 #include <vector>
@@ -54,7 +55,7 @@ using Clock = std::chrono::steady_clock;
 
 constexpr uint64_t kDefaultSlab = 256 * 1024;
 constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchange round
-constexpr uint64_t kDefaultSlotBytes = 256ull << 20;  // pinned bytes per slab when staging from files
+constexpr uint64_t kDefaultSlotBytes = 512ull << 20;  // pinned bytes per slab when staging from files
 constexpr uint64_t kDefaultRingSlots = 4;            // slabs read ahead when staging from files
 
 // The local extraction copy of a load runs while the leaf hash is still going.
@@ -207,10 +208,11 @@ struct tcx_group {
   // Peer view mappings for the push exchange (CUDA IPC), re-validated on every load.
   struct PeerView {
     cudaIpcMemHandle_t handle{};
-    void* base = nullptr;  // mapped allocation base in this process
+    void* base = nullptr;  // allocation base, mapped into this process (or the peer's own pointer)
     uint64_t offset = 0;   // view start inside the peer's allocation
     uint64_t size = 0;     // peer's view bytes
-    bool open = false;
+    bool open = false;     // an opened IPC mapping (another process's memory)
+    bool local = false;    // the peer is a thread of this process: its pointer is used as is
   };
   std::vector<PeerView> peer_views;
   // One stream per peer for the push copies (copy engines), so the pushes to
@@ -294,9 +296,23 @@ struct IpcRecord {
   uint64_t offset;            // view start inside that allocation
   uint64_t size;              // view bytes
   uint64_t valid;
-  uint64_t pad;
+  uint64_t process;           // token of the advertising process (same token: a thread of this process)
+  uint64_t base;              // allocation base in the advertising process
+  uint64_t device;            // the advertising rank's CUDA device
 };
-static_assert(sizeof(IpcRecord) == 96, "IPC record layout");
+static_assert(sizeof(IpcRecord) == 112, "IPC record layout");
+
+// A random token that tells this process apart from every other one on the node
+// (ranks that are threads of one process share memory without CUDA IPC, which
+// cannot open a handle exported by the same process).
+uint64_t process_token() {
+  static const uint64_t token = [] {
+    std::random_device rd;
+    uint64_t t = (static_cast<uint64_t>(rd()) << 32) ^ rd() ^ static_cast<uint64_t>(getpid());
+    return t == 0 ? 1 : t;
+  }();
+  return token;
+}
 
 // Stream-ordered barrier: completes on every rank only after every rank's earlier
 // work on its comm stream has completed.
@@ -329,6 +345,9 @@ tcx_status map_peer_views(tcx_group* g, void* d_view, uint64_t view_bytes, Clock
   mine.offset = offset;
   mine.size = view_bytes;
   mine.valid = 1;
+  mine.process = process_token();
+  mine.base = static_cast<uint64_t>(base);
+  mine.device = static_cast<uint64_t>(g->device);
   const uint64_t rec = sizeof(IpcRecord), world = static_cast<uint64_t>(g->world);
   tcx_status st;
   if ((st = g->ipc_records.grow((world + 1) * rec)) != TCX_OK) return st;
@@ -349,9 +368,30 @@ tcx_status map_peer_views(tcx_group* g, void* d_view, uint64_t view_bytes, Clock
     std::memcpy(&r, g->h_ipc + static_cast<uint64_t>(p) * rec, rec);
     if (!r.valid) return set_errorf(TCX_INTERNAL, "rank %d sent no view handle", p);
     auto& pv = g->peer_views[p];
-    if (!pv.open || std::memcmp(&pv.handle, &r.handle, sizeof r.handle) != 0) {
+    if (r.process == mine.process) {
+      // A thread of this process: write through its own pointer (unified addressing)
+      // once this device may access the peer's.
       if (pv.open) cudaIpcCloseMemHandle(pv.base);
       pv.open = false;
+      if (!pv.local || pv.base != reinterpret_cast<void*>(r.base)) {
+        const int peer_dev = static_cast<int>(r.device);
+        if (peer_dev != g->device) {
+          int can = 0;
+          TCX_CUDA_TRY(cudaDeviceCanAccessPeer(&can, g->device, peer_dev));
+          if (can) {
+            const cudaError_t e = cudaDeviceEnablePeerAccess(peer_dev, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+              return set_errorf(TCX_INTERNAL, "cudaDeviceEnablePeerAccess(%d): %s", peer_dev, cuda_msg(e).c_str());
+            cudaGetLastError();
+          }
+        }
+        pv.base = reinterpret_cast<void*>(r.base);
+        pv.local = true;
+      }
+    } else if (!pv.open || std::memcmp(&pv.handle, &r.handle, sizeof r.handle) != 0) {
+      if (pv.open) cudaIpcCloseMemHandle(pv.base);
+      pv.open = false;
+      pv.local = false;
       TCX_CUDA_TRY(cudaIpcOpenMemHandle(&pv.base, r.handle, cudaIpcMemLazyEnablePeerAccess));
       pv.handle = r.handle;
       pv.open = true;
@@ -475,6 +515,59 @@ extern "C" tcx_status tcx_group_create(const uint8_t* unique_id, int world, int 
   return TCX_OK;
 }
 
+namespace {
+// In-process rendezvous of tcx_group_join: the first rank thread of a group id
+// creates the NCCL unique id, the others take it; an entry lives until every rank
+// has taken it or its deadline passes (a later join of the same id then starts a
+// new generation).
+struct JoinEntry {
+  uint8_t uid[TCX_UNIQUE_ID_BYTES];
+  int world = 0;
+  std::vector<bool> taken;
+  int n_taken = 0;
+  Clock::time_point expires;
+};
+std::mutex g_join_mu;
+std::map<std::string, JoinEntry> g_joins;
+}  // namespace
+
+extern "C" tcx_status tcx_group_join(const char* group_id, int world, int rank, int device, int64_t timeout_ms,
+                                     tcx_group** out) {
+  if (out == nullptr) return set_error(TCX_INVALID_ARGUMENT, "out is null");
+  *out = nullptr;
+  if (group_id == nullptr) return set_error(TCX_INVALID_ARGUMENT, "group_id is null");
+  if (world < 1 || rank < 0 || rank >= world) return set_error(TCX_INVALID_ARGUMENT, "rank/world out of range");
+  if (world == 1) return tcx_group_create(nullptr, 1, 0, device, timeout_ms, out);
+  uint8_t uid[TCX_UNIQUE_ID_BYTES];
+  {
+    std::lock_guard<std::mutex> lk(g_join_mu);
+    const auto now = Clock::now();
+    auto it = g_joins.find(group_id);
+    if (it != g_joins.end() && now > it->second.expires) {
+      g_joins.erase(it);
+      it = g_joins.end();
+    }
+    if (it == g_joins.end()) {
+      JoinEntry e;
+      tcx_status st = tcx_group_unique_id(e.uid);
+      if (st != TCX_OK) return st;
+      e.world = world;
+      e.taken.assign(world, false);
+      e.expires = now + std::chrono::milliseconds(timeout_ms > 0 ? timeout_ms : 60000);
+      it = g_joins.emplace(group_id, std::move(e)).first;
+    }
+    JoinEntry& e = it->second;
+    if (e.world != world)
+      return set_errorf(TCX_INVALID_ARGUMENT, "group %s is being joined with world sizes %d and %d", group_id,
+                        e.world, world);
+    if (e.taken[rank]) return set_errorf(TCX_INVALID_ARGUMENT, "rank %d of group %s joined twice", rank, group_id);
+    e.taken[rank] = true;
+    std::memcpy(uid, e.uid, sizeof uid);
+    if (++e.n_taken == world) g_joins.erase(it);
+  }
+  return tcx_group_create(uid, world, rank, device, timeout_ms, out);
+}
+
 extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   if (g == nullptr) return TCX_OK;
   cudaSetDevice(g->device);
@@ -492,7 +585,7 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   for (cudaStream_t s : g->s_peer)
     if (s) cudaStreamSynchronize(s);
   for (auto& pv : g->peer_views)
-    if (pv.open) cudaIpcCloseMemHandle(pv.base);
+    if (pv.open && !pv.local) cudaIpcCloseMemHandle(pv.base);
   g->peer_views.clear();
   for (cudaEvent_t e : g->peer_done)
     if (e) cudaEventDestroy(e);

@@ -1,6 +1,7 @@
 """Collective load: Python face of tcx_group_* (include/tcx.h).
 
-A ``Group`` is one rank of an N-rank load, one process per GPU. Ranks agree on a
+A ``Group`` is one rank of an N-rank load: one process per GPU (``from_torch_distributed``)
+or one thread per GPU in one process (``join``, the reference daemon's model). Ranks agree on a
 leaf-aligned split of the canonical byte space (``stage_bounds``); each stages its
 part, hashes the leaves it staged, and the native engine exchanges exactly the bytes
 each peer's view needs (NCCL grouped send/recv). All ranks end with their view and
@@ -148,6 +149,17 @@ class Group:
                 raise ValueError("a 128-byte NCCL unique id is required for world > 1")
             uid = ctypes.create_string_buffer(bytes(unique_id), 128)
         _native.call("tcx_group_create", uid, world, rank, device, int(timeout_ms), ctypes.byref(self._h))
+
+    @classmethod
+    def join(cls, group_id: str, world: int, rank: int, device: int, timeout_ms: int = 120_000) -> "Group":
+        """Joins rank `rank` of group `group_id` from a thread of this process (tcx_group_join):
+        the rank threads of one process find each other by the id, no launcher or store needed."""
+        g = cls.__new__(cls)
+        g.world, g.rank, g.device = world, rank, device
+        g._h = ctypes.c_void_p()
+        _native.call("tcx_group_join", str(group_id).encode(), int(world), int(rank), int(device), int(timeout_ms),
+                     ctypes.byref(g._h))
+        return g
 
     @staticmethod
     def unique_id() -> bytes:

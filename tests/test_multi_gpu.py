@@ -1,7 +1,9 @@
 """N>1 paths.
 
 * GPU (marked gpu): tests/mp_load_worker.py on 2 (and, when present, 4) GPUs through
-  torch.distributed.run + NCCL: every rank's view and the Merkle root against the oracles.
+  torch.distributed.run + NCCL: every rank's view and the Merkle root against the oracles;
+  tests/threads_load_worker.py: the same cases with the ranks as threads of one process
+  (tcx_group_join, the reference daemon's model), plus the SDK path from those threads.
 * CPU (gloo, world size 2): the host side of a collective load in two real processes:
   every rank's view jobs travel through gather_rank_jobs (all_gather_object), each rank
   computes its exchange schedule with the native planner, packs its share in numpy,
@@ -41,6 +43,49 @@ def test_collective_load_parity_multi_gpu(world):
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "failures=0" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4])
+def test_collective_load_parity_rank_threads(world):
+    """The same loads with the ranks as threads of one process (tcx_group_join)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs, {torch.cuda.device_count()} visible")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, os.path.join(HERE, "threads_load_worker.py"), str(world)]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=700)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert f"world={world} failures=0 errors=0" in r.stdout
+
+
+def test_in_process_job_gather_rounds():
+    """The in-process all-gather the rank threads use for their view jobs: every thread gets
+    every rank's bytes in rank order, over several rounds under one group id."""
+    import threading
+    from tensorcast_b200.api import _gather_in_process
+    world, rounds = 3, 4
+    got = {}
+
+    def rank(r):
+        for k in range(rounds):
+            got[(r, k)] = _gather_in_process("g-test", world, r, f"{r}:{k}".encode())
+
+    ts = [threading.Thread(target=rank, args=(r,)) for r in range(world)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(timeout=30)
+    for r in range(world):
+        for k in range(rounds):
+            assert got[(r, k)] == [f"{q}:{k}".encode() for q in range(world)]
+
+
+def test_in_process_job_gather_times_out_without_peers():
+    from tensorcast_b200.api import ArtifactError, _gather_in_process
+    from tensorcast_b200 import api
+    with pytest.raises(ArtifactError, match="timed out"):
+        _gather_in_process("g-lonely", 2, 0, b"x", timeout_s=0.2)
+    assert "g-lonely" not in api._RDV_TABLE
 
 
 def _gloo_rank(rank: int, world: int, port: int, q) -> None:
