@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's own GPU kernel")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the extra legs after the main line (paged KV; bind_into at N>1; disk-dir hash at N=1)")
     ap.add_argument("--exchange", choices=["auto", "push", "nccl", "allgather"], default="auto",
                     help="N>1 shard exchange: push over peer memory (copy-engine copies into the peers' views "
                          "over NVLink) or NCCL send/recv of packed windows; auto = push for the Llama-3-8B "
@@ -673,15 +675,50 @@ def main() -> None:
             line["cpu_baseline"] = cpu
         if ref_gpu is not None:
             line["reference_gpu_kernel"] = ref_gpu
+        if world > 1:
+            # The shard exchange of the device-resident steps (it runs beside the hash).
+            gbs = peer / exch_ms / 1e6 if exch_ms > 0 else 0.0
+            line["exchange"] = {"mode": exchange_mode(args), "recv_bytes_per_rank": int(peer),
+                                "exchange_and_view_ms": round(exch_ms, 3), "gbs_per_rank": round(gbs, 1),
+                                "frac_of_nvlink_900": round(gbs / 900.0, 4),
+                                "frac_of_measured_peer_copy_770": round(gbs / 770.0, 4),
+                                "note": "received bytes per rank / the exchange-and-view phase of a device-resident "
+                                        "step; the phase overlaps the leaf hash, which bounds the step"}
+
+    # Extra legs (driver-visible evidence of the other benchmark rows), after the main
+    # workload's buffers are released: paged KV (config 5) on every N, the collective
+    # bind_into at N > 1, the disk-directory hash at N = 1.
+    extras = {}
+    if not args.no_extras:
+        del d_view, d_stage, h_stage, first, file_res, e2e_res, steps
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        barrier()
+        if world > 1:
+            extras["bind_into"] = bind_into_check(args, path, index, world, rank, local)
+        try:
+            extras["kv"] = kv_measure(args, world, rank, local)
+        except torch.OutOfMemoryError as e:
+            extras["kv"] = {"unavailable": f"device memory: {e}"[:300]}
+        if world == 1:
+            extras["disk_hash"] = measure_disk_hash(args, min(args.steps, 5), 1)
+    bad = []
+    if rank == 0:
+        line.update({k: v for k, v in extras.items() if v is not None})
         print(json.dumps(line), flush=True)
+        bad = [k for k, v in extras.items() if isinstance(v, dict) and
+               (v.get("ok") is False or v.get("matches_cpu_oracle") is False or
+                v.get("parity", {}).get("first_and_last_shard_sequences_match_oracle") is False)]
     group.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if bad:
+        raise SystemExit(f"PARITY FAILURE in {bad}")
 
 
-def run_kv(args) -> None:
-    """The paged-KV benchmark: 64 planes (32 layers x K/V) of 65536 pages [16, 8, 128] bf16 (seed 3),
+def kv_measure(args, world: int, rank: int, local: int):
+    """The paged-KV benchmark (BASELINE config 5): 64 planes (32 layers x K/V) of 65536 pages [16, 8, 128] bf16 (seed 3),
     sequences of 64-4096 tokens drawn in order until the pool is full, pages at a seeded
     permutation; the sequences are dealt to 8 shards and rank r processes shards r, r+N, ...
     (each shard's pool holds its own pages in their global random order). A step gathers
@@ -693,14 +730,6 @@ def run_kv(args) -> None:
     from tensorcast_b200 import _native, kvcache
     from oracle import kv as okv
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
     w = kvcache.workload(seed=3)
     shards = [w.shard(8, k, local_pool=True) for k in range(rank, 8, world)]
     pools, runners = [], []
@@ -786,21 +815,101 @@ def run_kv(args) -> None:
         ms, total, ok = float(mx[0]), float(sm[1]), bool(mn[2] > 0)
     else:
         total = float(mine)
+    del runners, pools, shared
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {"value": round(total / ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(ms, 3),
+            "steps": args.steps, "warmup": args.warmup,
+            "config": {"workload": "paged KV: 64 planes x 65536 pages [16, 8, 128] bf16, seed 3, "
+                                   f"{w.n_seq} sequences (64-4096 tokens), 2 MiB leaves, 8 sequence shards "
+                                   "dealt to the ranks",
+                       "gathered_bytes": int(total), "sequences": w.n_seq,
+                       "pipeline": f"{n_buf} output buffer(s) / stream(s) per rank"},
+            "parity": {"first_and_last_shard_sequences_match_oracle": ok},
+            "gpu_launches": int(launches), "clocks": clk.summary()}
+
+
+def run_kv(args) -> None:
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    out = kv_measure(args, world, rank, local)
     if rank == 0:
-        line = {"metric": "Paged-KV gather + per-sequence SHA-256 GB/s (config 5)", "value": round(total / ms / 1e6, 2),
-                "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "u32", "data": "synthetic",
-                "config": {"workload": "paged KV: 64 planes x 65536 pages [16, 8, 128] bf16, seed 3, "
-                                       f"{w.n_seq} sequences (64-4096 tokens), 2 MiB leaves, 8 sequence shards",
-                           "gathered_bytes": int(total), "sequences": w.n_seq,
-                           "pipeline": f"{n_buf} output buffer(s) / stream(s) per rank"},
-                "parity": {"first_and_last_shard_sequences_match_oracle": ok},
-                "gpu_launches": int(launches), "clocks": clk.summary()}
+        line = {"metric": "Paged-KV gather + per-sequence SHA-256 GB/s (config 5)", "n_gpus": world,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32",
+                "data": "synthetic"}
+        line.update(out)
         print(json.dumps(line), flush=True)
+        if not out["parity"]["first_and_last_shard_sequences_match_oracle"]:
+            raise SystemExit("PARITY FAILURE: paged-KV gather or hash differs from the oracle")
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def measure_disk_hash(args, steps: int, warmup: int) -> dict:
+    """compute_data_multihash_from_disk_dir (disk_dir_hash.cc:47-104) of a directory holding
+    the artifact, on this rank's GPU: preads into pinned slots, H2D and the leaf kernel per
+    1 GiB group of 4 MiB leaves, Merkle root on the GPU; wall-clock timed (the call is
+    synchronous), checked against the CPU oracle over the same payload bytes."""
+    import numpy as np
+    from oracle import oracle
+    from tensorcast_b200.disk_hash import compute_data_multihash_from_disk_dir
+    path = artifact_path(args)
+    d = os.path.join(args.dir, f"dirhash-{args.model}")
+    os.makedirs(d, exist_ok=True)
+    link = os.path.join(d, "model.safetensors")
+    if not os.path.islink(link):
+        os.symlink(path, link)
+    with open(path + ".done") as f:
+        info = json.load(f)
+    T = info["total_bytes"]
+    got = None
+    for _ in range(warmup):
+        got = compute_data_multihash_from_disk_dir(d)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        got = compute_data_multihash_from_disk_dir(d)
+        times.append(time.perf_counter() - t0)
+    raw = np.memmap(path, dtype=np.uint8, mode="r", offset=info["payload_offset"], shape=(T,))
+    want = oracle.multihash(oracle.tree_root(oracle.leaf_digests(raw, LEAF, openssl=True,
+                                                                 threads=min(32, os.cpu_count() or 1))))
+    ms = statistics.median(times) * 1e3
+    return {"value": round(T / ms / 1e6, 2), "unit": "GB/s", "ms_per_call": round(ms, 1), "steps": steps,
+            "config": {"workload": f"compute_data_multihash_from_disk_dir of a directory holding the {args.model} "
+                                   f"safetensors file ({T} B payload, 4 MiB leaves, page-cache-hot tmpfs)",
+                       "timing": "wall clock of the synchronous call"},
+            "multihash": got, "matches_cpu_oracle": got == want}
+
+
+def run_disk_hash(args) -> None:
+    import torch
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    torch.cuda.set_device(0)
+    path = ensure_artifact(args, 0, 0)
+    out = measure_disk_hash(args, args.steps, args.warmup)
+    with open(path + ".done") as f:
+        info = json.load(f)
+    cpu = None if args.no_cpu_baseline else cpu_reference_sample(path, info["payload_offset"], info["total_bytes"],
+                                                                 LEAF, args.cpu_seconds)
+    line = {"metric": "compute_data_multihash_from_disk_dir GB/s (tmpfs -> GPU SHA-256)", "n_gpus": 1,
+            "warmup": args.warmup, "higher_is_better": True, "cpu_baseline": cpu}
+    line.update(out)
+    print(json.dumps(line), flush=True)
+    if not out["matches_cpu_oracle"]:
+        raise SystemExit("disk-dir multihash differs from the CPU oracle")
+
+
 
 
 def verify_view_full(path, index, plan, d_view, world, rank, transposed=None):
@@ -831,6 +940,66 @@ def verify_view_full(path, index, plan, d_view, world, rank, transposed=None):
     with ThreadPoolExecutor(max(2, min(16, len(os.sched_getaffinity(0))))) as ex:
         res = list(ex.map(check, plan.tensors))
     return all(r[0] for r in res), sum(r[1] for r in res), len(res)
+
+
+def bind_into_check(args, path, index, world, rank, local) -> dict:
+    """The collective bind_into of the SDK (Artifact.view(...).bind_into(targets, ctx=...),
+    the reference's mapped-target load, collective_disk_loader.cc:5818-6293): every rank's
+    tensor-parallel view straight into one separate CUDA tensor per tensor, through the
+    NCCL shard exchange; every target compared byte for byte with numpy slicing of the file.
+    Returns the result on rank 0 (all ranks take part)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from tensorcast_b200 import api
+    from tensorcast_b200.artifact import ELEMENT_SIZE
+    slices = tp_slices(index, world, rank)
+    view_slices = {n: (sl if d == 0 else (1, sl)) for n, (d, sl) in slices.items()}
+    art = api.from_disk(path).view(slices=view_slices)
+    udt = {1: np.uint8, 2: np.uint16, 4: np.uint32, 8: np.uint64}
+    dts = {"torch.bfloat16": torch.bfloat16, "torch.float16": torch.float16, "torch.float32": torch.float32}
+    targets = {}
+    for name, e in index.entries.items():
+        shape = list(e.shape)
+        if name in slices:
+            d, sl = slices[name]
+            shape[d] = sl.stop - sl.start
+        targets[name] = torch.empty(shape, dtype=dts.get(e.dtype, torch.bfloat16), device=f"cuda:{local}")
+    ctx = api.CallContext(collective=api.CollectiveLoadGroup("bench-bind-into", world, rank))
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    art.bind_into(targets, ctx=ctx)
+    torch.cuda.synchronize()
+    secs = time.perf_counter() - t0
+    bad, checked = 0, 0
+    for name, t in targets.items():
+        st, e = index.sources[name], index.entries[name]
+        arr = np.memmap(path, dtype=udt[ELEMENT_SIZE[e.dtype]], mode="r", offset=st.file_offset, shape=tuple(st.shape))
+        if name in slices:
+            d, sl = slices[name]
+            arr = arr[sl] if d == 0 else arr[:, sl]
+        want = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
+        got = t.reshape(-1).view(torch.uint8).cpu().numpy()
+        bad += 0 if np.array_equal(got, want) else 1
+        checked += got.size
+    r = torch.tensor([bad, checked, len(targets), secs], dtype=torch.float64, device="cuda")
+    mx = r.clone()
+    dist.all_reduce(r, op=dist.ReduceOp.SUM)
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    del targets
+    # Every rank releases the SDK's group here, at the same point (its NCCL finalize
+    # involves the peers).
+    for g in list(api._GROUPS.values()):
+        g.close()
+    api._GROUPS.clear()
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {"ok": int(r[0].item()) == 0, "targets_checked": int(r[2].item()), "bytes_checked": int(r[1].item()),
+            "seconds_max_over_ranks": round(float(mx[3].item()), 3),
+            "what": "SDK Artifact.view(TP-N slices).bind_into(one CUDA tensor per tensor, ctx=CollectiveLoadGroup) "
+                    "from the file: every target == numpy slicing of the file"}
 
 
 def straddling_tensors(index, bounds) -> int:
