@@ -52,14 +52,16 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU baseline sample time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's own GPU kernel")
+    ap.add_argument("--no-c4", action="store_true", help="at N>1, skip the Llama-3-70B (config 4) leg")
+    ap.add_argument("--c4-exchange", choices=["nccl", "push"], default="push",
+                    help="shard exchange of the config-4 leg (push: copy-engine copies into the peers' views, "
+                         "measured faster than NCCL send/recv on the 70B TP-2 load)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the extra legs after the main line (paged KV; bind_into at N>1; disk-dir hash at N=1)")
     ap.add_argument("--exchange", choices=["auto", "push", "nccl", "allgather"], default="auto",
                     help="N>1 shard exchange: push over peer memory (copy-engine copies into the peers' views "
-                         "over NVLink) or NCCL send/recv of packed windows; auto = push for the Llama-3-8B "
-                         "artifact (its exchange hides behind the hash), NCCL for the 70B one (measured faster "
-                         "where the exchange is the longer leg); allgather = windowed broadcast of every rank's "
-                         "staged bytes to all ranks (every rank sees every byte)")
+                         "over NVLink) or NCCL send/recv of packed windows; auto = push; allgather = windowed "
+                         "broadcast of every rank's staged bytes to all ranks (every rank sees every byte)")
     ap.add_argument("--stage", choices=["mapped", "pinned"], default="pinned",
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
                          "(no second host copy), or a pinned copy read with parallel preads")
@@ -78,9 +80,9 @@ def parse_args():
 
 
 def exchange_mode(args) -> str:
-    if args.exchange != "auto":
-        return args.exchange
-    return "nccl" if args.model == "llama3-70b" else "push"
+    # auto: the copy-engine push for both artifacts (with the local extraction on its own
+    # stream it measured faster than NCCL send/recv on the 70B TP-2 load: 127 against 154 ms)
+    return "push" if args.exchange == "auto" else args.exchange
 
 
 def _size(x: str) -> int:
@@ -550,6 +552,7 @@ def main() -> None:
     ms = max_over_ranks(statistics.mean(dev_ms))
     hash_ms = max_over_ranks(statistics.mean(r["hash_ms"] for r in steps))
     exch_ms = max_over_ranks(statistics.mean(r["exchange_ms"] for r in steps))
+    xfer_ms = max_over_ranks(statistics.mean(r["transfer_ms"] for r in steps))
     wall = max_over_ranks(wall)
 
     # e2e (headline): from the files through tcx_group_load_files -- preads into the
@@ -592,6 +595,7 @@ def main() -> None:
     # e2e bound: this run's own host-to-device rate, a plain pinned -> device copy of each
     # rank's staged range on all ranks at once (the same bytes d_stage already holds).
     h2d_peak = None
+    h2d_solo, read_solo = [0.0] * world, [0.0] * world
     if isinstance(h_stage, torch.Tensor):
         n = min(hi - lo, 4 << 30)
         s = torch.cuda.current_stream()
@@ -606,6 +610,25 @@ def main() -> None:
             t = max_over_ranks(c0.elapsed_time(c1))
             best = max(best, n * world / t / 1e6)
         h2d_peak = round(best, 2)
+        if world > 1:
+            # Each GPU alone (the others idle at a barrier), to tell a per-link limit from a
+            # shared host-side one, and the same for the preads of each rank's range.
+            for r in range(world):
+                barrier()
+                if r == rank:
+                    c0.record(s)
+                    d_stage[:n].copy_(h_stage[:n], non_blocking=True)
+                    c1.record(s)
+                    c1.synchronize()
+                    h2d_solo[r] = n / c0.elapsed_time(c1) / 1e6
+                    t0 = time.perf_counter()
+                    read_segments(files_mine, h_stage.data_ptr(), threads=read_threads)
+                    read_solo[r] = (hi - lo) / (time.perf_counter() - t0) / 1e9
+            barrier()
+            sv = torch.tensor(h2d_solo + read_solo, dtype=torch.float64, device="cuda")
+            dist.all_reduce(sv, op=dist.ReduceOp.SUM)
+            h2d_solo = [round(float(x), 2) for x in sv[:world].tolist()]
+            read_solo = [round(float(x), 2) for x in sv[world:].tolist()]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and canonical_is_payload:
@@ -646,6 +669,10 @@ def main() -> None:
                               "peak_gbs": h2d_peak,
                               "frac": round(T / file_ms / 1e6 / h2d_peak, 4) if h2d_peak else None,
                               "read_gbs": read_gbs,
+                              "h2d_gbs_per_gpu_alone": h2d_solo if world > 1 else None,
+                              "read_gbs_per_rank_alone": read_solo if world > 1 else None,
+                              "h2d_gbs_per_gpu_all_at_once": round(h2d_peak / world, 2) if h2d_peak else None,
+                              "read_gbs_per_rank_all_at_once": round(read_gbs / world, 2) if read_gbs else None,
                               "frac_of_min_h2d_read": round(T / file_ms / 1e6 / min(h2d_peak, read_gbs), 4)
                               if h2d_peak and read_gbs else None,
                               "source": "measured in this run: pinned -> device copy of each rank's staged range, "
@@ -677,13 +704,7 @@ def main() -> None:
             line["reference_gpu_kernel"] = ref_gpu
         if world > 1:
             # The shard exchange of the device-resident steps (it runs beside the hash).
-            gbs = peer / exch_ms / 1e6 if exch_ms > 0 else 0.0
-            line["exchange"] = {"mode": exchange_mode(args), "recv_bytes_per_rank": int(peer),
-                                "exchange_and_view_ms": round(exch_ms, 3), "gbs_per_rank": round(gbs, 1),
-                                "frac_of_nvlink_900": round(gbs / 900.0, 4),
-                                "frac_of_measured_peer_copy_770": round(gbs / 770.0, 4),
-                                "note": "received bytes per rank / the exchange-and-view phase of a device-resident "
-                                        "step; the phase overlaps the leaf hash, which bounds the step"}
+            line["exchange"] = exchange_summary(exchange_mode(args), peer, exch_ms, xfer_ms)
 
     # Extra legs (driver-visible evidence of the other benchmark rows), after the main
     # workload's buffers are released: paged KV (config 5) on every N, the collective
@@ -694,8 +715,19 @@ def main() -> None:
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         barrier()
+        torch._C._host_emptyCache()  # release the pinned staging copy to the host
+        # The main group goes first (all ranks at once): it also closes its peer-view
+        # mappings, so the views freed above are returned to their devices.
+        group.close()
+        torch.cuda.empty_cache()
         if world > 1:
             extras["bind_into"] = bind_into_check(args, path, index, world, rank, local)
+            if args.model == "llama3-8b" and not args.no_c4:
+                g4 = Group.from_torch_distributed(local)
+                try:
+                    extras["c4"] = c4_leg(args, g4, world, rank, local, read_threads, args.c4_exchange)
+                finally:
+                    g4.close()
         try:
             extras["kv"] = kv_measure(args, world, rank, local)
         except torch.OutOfMemoryError as e:
@@ -940,6 +972,151 @@ def verify_view_full(path, index, plan, d_view, world, rank, transposed=None):
     with ThreadPoolExecutor(max(2, min(16, len(os.sched_getaffinity(0))))) as ex:
         res = list(ex.map(check, plan.tensors))
     return all(r[0] for r in res), sum(r[1] for r in res), len(res)
+
+
+def exchange_summary(mode: str, recv: float, phase_ms: float, xfer_ms: float) -> dict:
+    """The shard exchange of the device-resident steps, per rank: bytes received over the
+    transfer itself (pushes or NCCL rounds, device events) as a fraction of NVLink 5 (900 GB/s
+    per direction) and of the measured 770 GB/s peer copy; the phase also holds the local
+    extraction and runs beside the leaf hash."""
+    gbs = recv / xfer_ms / 1e6 if xfer_ms > 0 else 0.0
+    return {"mode": mode, "recv_bytes_per_rank": int(recv), "transfer_ms": round(xfer_ms, 3),
+            "gbs_per_rank": round(gbs, 1), "frac_of_nvlink_900": round(gbs / 900.0, 4),
+            "frac_of_measured_peer_copy_770": round(gbs / 770.0, 4), "exchange_and_view_ms": round(phase_ms, 3),
+            "note": "received bytes per rank / the device time of the transfer (max over ranks); it runs beside the "
+                    "leaf hash and the local extraction"}
+
+
+def host_mem_available() -> int:
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+def c4_leg(args, group, world: int, rank: int, local: int, read_threads: int, exchange: str = "nccl"):
+    """BASELINE config 4 at N > 1: the Llama-3-70B-shaped artifact (141.1 GB, seed 2) with
+    TP-N views plus the layer-0 o_proj stored [in, out] and read through a transpose view,
+    over the NCCL shard exchange. Runs when the host can hold the file in tmpfs and every
+    GPU its share and view; otherwise returns a skip reason. Parity: the root against the
+    CPU oracle over the whole file and every byte of every rank's view against numpy
+    slicing of the file. value: device-resident steps; e2e: from the file, as the main line."""
+    import copy
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from tensorcast_b200.artifact import build_canonical_index, build_source_index, canonical_segments
+    from tensorcast_b200.loader import stage_bounds
+    from tensorcast_b200.synthetic import artifact_bytes
+    from tensorcast_b200.views import build_view_spec, plan_view
+    a70 = copy.copy(args)
+    a70.model = "llama3-70b"
+    shapes = model_shapes(a70.model)
+    need = artifact_bytes(shapes)
+    path = artifact_path(a70)
+    exists = os.path.exists(path + ".done")
+    st = os.statvfs(args.dir) if os.path.isdir(args.dir) else None
+    shm_free = st.f_bavail * st.f_frsize if st else 0
+    host_ok = (exists or shm_free > need + (4 << 30)) and \
+        host_mem_available() > (0 if exists else need) + world * (3 << 30) + (48 << 30)
+    gpu_ok = torch.cuda.mem_get_info()[0] > 2.3 * need / world
+    flags = torch.tensor([1.0 if host_ok else 0.0, 1.0 if gpu_ok else 0.0], dtype=torch.float64, device="cuda")
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    if flags.min().item() < 1:
+        return {"skipped": f"needs {need / 1e9:.1f} GB of tmpfs and host memory for the file "
+                           f"(host ok: {bool(flags[0].item())}) and ~{2.3 * need / world / 1e9:.0f} GB free per GPU "
+                           f"(gpu ok: {bool(flags[1].item())})"} if rank == 0 else None
+    t0 = time.perf_counter()
+    ensure_artifact(a70, rank, local, world)
+    gen_s = time.perf_counter() - t0
+    index = build_canonical_index(build_source_index(path))
+    T, L = index.total_bytes, args.leaf
+    bounds = stage_bounds(T, L, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    plans = []
+    for r in range(world):
+        slices = tp_slices(index, world, r)
+        slices.pop(TRANSPOSED_O_PROJ, None)
+        plans.append(plan_view(index, build_view_spec(index, slices=slices,
+                                                      transpose={TRANSPOSED_O_PROJ: [(0, 1)]})))
+    mine = plans[rank]
+    rank_jobs = [p.jobs for p in plans]
+    files = canonical_segments(index, lo, hi)
+    d_stage = torch.empty(hi - lo, dtype=torch.uint8, device="cuda")
+    d_view = torch.empty(max(mine.view_bytes, 1), dtype=torch.uint8, device="cuda")
+
+    def load(from_files: bool, expected=None):
+        return group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view,
+                          files=files if from_files else None, read_threads=read_threads,
+                          permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected,
+                          peer_push=exchange == "push")
+
+    def mx(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    first = load(True)
+    root = first["root"]
+    root_ok = True
+    if rank == 0:
+        from oracle import oracle
+        whole = canonical_segments(index, 0, T)
+        if len(whole) == 1 and whole[0][3] == T:
+            mm = np.memmap(path, dtype=np.uint8, mode="r", offset=whole[0][1], shape=(T,))
+            root_ok = oracle.tree_root(oracle.leaf_digests(mm, L, openssl=True, threads=os.cpu_count() or 8)) == root
+            del mm
+    view_ok, checked, n_t = verify_view_full(path, index, mine, d_view, world, rank, TRANSPOSED_O_PROJ)
+    agg = torch.tensor([1.0 if view_ok else 0.0, 1.0 if root_ok else 0.0, checked, n_t], dtype=torch.float64,
+                       device="cuda")
+    mn = agg.clone()
+    dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+    dist.all_reduce(agg, op=dist.ReduceOp.SUM)
+    # value: device-resident steps
+    load(False, root)
+    dist.barrier()
+    torch.cuda.synchronize()
+    res = [load(False, root) for _ in range(2)]
+    ms = mx(statistics.mean(r["total_ms"] for r in res))
+    hash_ms = mx(statistics.mean(r["hash_ms"] for r in res))
+    exch_ms = mx(statistics.mean(r["exchange_ms"] for r in res))
+    xfer_ms = mx(statistics.mean(r["transfer_ms"] for r in res))
+    recv = mx(float(res[-1]["peer_recv_bytes"]))
+    # e2e: from the file
+    cur = torch.cuda.current_stream()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    load(True, root)
+    dist.barrier()
+    torch.cuda.synchronize()
+    f0.record(cur)
+    fres = [load(True, root) for _ in range(2)]
+    f1.record(cur)
+    f1.synchronize()
+    file_ms = mx(f0.elapsed_time(f1) / 2)
+    read_ms = mx(statistics.mean(r["stage_read_ms"] for r in fres))
+    del d_stage, d_view
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {"workload": f"llama3-70b-shaped bf16 safetensors (seed 2), {T} B, TP-{world} views + {TRANSPOSED_O_PROJ} "
+                        "stored [in, out] read whole through a transpose view; "
+                        + ("copy-engine push" if exchange == "push" else "NCCL send/recv shard exchange"),
+            "artifact_bytes": T, "leaves": first["leaves"], "view_bytes_per_rank": mine.view_bytes,
+            "value": round(T / ms / 1e6, 2), "ms_per_step": round(ms, 3), "steps": 2, "warmup": 1,
+            "phases_ms": {"hash": round(hash_ms, 3), "exchange_and_view": round(exch_ms, 3)},
+            "e2e": {"value": round(T / file_ms / 1e6, 2), "ms_per_step": round(file_ms, 3),
+                    "stage_read_ms": round(read_ms, 3), "steps": 2, "warmup": 1,
+                    "from": "the file in tmpfs, tcx_group_load_files on every rank"},
+            "exchange": exchange_summary(exchange, recv, exch_ms, xfer_ms),
+            "parity": {"root_matches_cpu_oracle": bool(mn[1].item() > 0), "view_full_ok": bool(mn[0].item() > 0),
+                       "view_bytes_checked": int(agg[2].item()), "view_tensors_checked": int(agg[3].item()),
+                       "multihash": first["multihash"]},
+            "ok": bool(mn[0].item() > 0 and mn[1].item() > 0),
+            "artifact_write_s": round(gen_s, 1)}
 
 
 def bind_into_check(args, path, index, world, rank, local) -> dict:

@@ -276,6 +276,10 @@ typedef struct tcx_load_plan {
   const uint64_t* target_ranges; /* TCX_LOAD_TARGETS: n_targets (offset, length) pairs of this
                                     rank's view space that are writable; NULL otherwise */
   uint64_t n_targets;
+  uint64_t push_nccl_permille;   /* with TCX_LOAD_PEER_PUSH: this share (per mille, whole pieces in
+                                    view order) of every (sender, receiver) pair's bytes goes over
+                                    NCCL send/recv at the same time as the copy engines push the rest
+                                    (0: the copy engines carry everything) */
 } tcx_load_plan;
 
 /* tcx_load_plan.flags: also compute the data multihash of this rank's finished
@@ -455,6 +459,7 @@ typedef struct tcx_load_result {
   char view_multihash[64];  /* with TCX_LOAD_VIEW_HASH: data multihash of this rank's view, else "" */
   uint64_t view_leaf_bytes; /* leaf size used for view_multihash */
   float stage_read_ms;      /* tcx_group_load_files: host time from the first read to the last slab read */
+  float transfer_ms;        /* device time of this rank's peer transfer: its pushes, or the NCCL rounds */
 } tcx_load_result;
 
 /* Runs one collective load on every rank of g (all ranks call it with the same

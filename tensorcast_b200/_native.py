@@ -75,7 +75,7 @@ class LoadPlan(ctypes.Structure):
                 ("jobs", _c.c_void_p), ("job_offsets", _c.c_void_p), ("permutes", _c.c_void_p),
                 ("n_permutes", _c.c_uint64), ("view_bytes", _c.c_uint64), ("slab_bytes", _c.c_uint64),
                 ("window_bytes", _c.c_uint64), ("flags", _c.c_uint64), ("target_ranges", _c.c_void_p),
-                ("n_targets", _c.c_uint64)]
+                ("n_targets", _c.c_uint64), ("push_nccl_permille", _c.c_uint64)]
 
 
 class ExchangePlan(ctypes.Structure):
@@ -91,7 +91,7 @@ class LoadResult(ctypes.Structure):
                 ("h2d_bytes", _c.c_uint64), ("peer_send_bytes", _c.c_uint64), ("peer_recv_bytes", _c.c_uint64),
                 ("h2d_ms", _c.c_float), ("hash_ms", _c.c_float), ("exchange_ms", _c.c_float),
                 ("total_ms", _c.c_float), ("view_multihash", _c.c_char * 64), ("view_leaf_bytes", _c.c_uint64),
-                ("stage_read_ms", _c.c_float)]
+                ("stage_read_ms", _c.c_float), ("transfer_ms", _c.c_float)]
 
 
 class FileStage(ctypes.Structure):

@@ -30,6 +30,7 @@
 #include <chrono>
 #include <condition_variable>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <deque>
 #include <functional>
@@ -67,9 +68,28 @@ constexpr uint64_t kDefaultRingSlots = 4;            // slabs read ahead when st
 // that the hash is throughput-bound like the copy, which keeps the full grid.
 // (The NCCL path's pack and scatter kernels keep the full grid: they gate the
 // exchange, which is the longer leg of the 70B loads at N=2 and 4.)
-uint32_t load_copy_ctas(uint64_t n_chains) {
+// The cap applies only while the capped copy still ends inside the hash: measured
+// on the Llama-3-70B TP-2 load (16.8k chains, 35 GB of local pieces per rank), the
+// quarter grid moved about 220 GB/s and set the step (159 ms against a 125 ms hash),
+// while the full grid finished beside the hash (step 127 ms, hash unchanged). So the
+// full grid is used once the local bytes at 220 GB/s would take more than 60% of one
+// chain's time (about 1 us per 64-byte block).
+uint32_t load_copy_ctas(uint64_t n_chains, uint64_t local_bytes, uint64_t leaf_bytes) {
+  // TCX_LOCAL_COPY_CTAS overrides the cap (0 = the full grid) for measurements.
+  if (const char* v = std::getenv("TCX_LOCAL_COPY_CTAS")) return static_cast<uint32_t>(std::strtoul(v, nullptr, 10));
   const uint64_t sms = static_cast<uint64_t>(sm_count());
-  return n_chains < sms * 128 ? static_cast<uint32_t>(std::max<uint64_t>(8, sms / 4)) : 0u;
+  if (n_chains >= sms * 128) return 0u;
+  const double chain_s = static_cast<double>(leaf_bytes / 64) * 1e-6;
+  const double capped_s = static_cast<double>(local_bytes) / 220e9;
+  if (capped_s > 0.6 * chain_s) return 0u;
+  return static_cast<uint32_t>(std::max<uint64_t>(8, sms / 4));
+}
+
+// TCX_LOCAL_COPY=ce moves this rank's own view pieces with the copy engines (one
+// 2-D copy per piece) instead of the copy kernel (measurement knob).
+bool local_copy_on_copy_engines() {
+  const char* v = std::getenv("TCX_LOCAL_COPY");
+  return v != nullptr && std::strcmp(v, "ce") == 0;
 }
 
 std::string nccl_msg(ncclResult_t r) { return std::string(ncclGetErrorString(r)); }
@@ -198,6 +218,9 @@ struct tcx_group {
   int64_t timeout_ms = 60000;
   ncclComm_t comm = nullptr;
   cudaStream_t s_copy = nullptr, s_hash = nullptr, s_comm = nullptr, s_pack = nullptr;
+  cudaStream_t s_local = nullptr;  // this rank's own view pieces, beside the exchange (world > 1)
+  cudaEvent_t ev_local = nullptr;
+  cudaEvent_t ev_xfer0 = nullptr, ev_xfer1 = nullptr;  // timed: the peer transfer (pushes or NCCL rounds)
   DevBuf digests_mine, states, digests_all, digests_compact, merkle_scratch, root, send, recv, perm_scratch, jobs,
       prefix, view_digests, view_scratch;
   uint8_t* h_root = nullptr;
@@ -494,9 +517,11 @@ extern "C" tcx_status tcx_group_create(const uint8_t* unique_id, int world, int 
   if (cudaStreamCreateWithFlags(&g->s_copy, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&g->s_hash, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&g->s_comm, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&g->s_pack, cudaStreamNonBlocking) != cudaSuccess)
+      cudaStreamCreateWithFlags(&g->s_pack, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&g->s_local, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&g->ev_local, cudaEventDisableTiming) != cudaSuccess)
     return fail(set_error(TCX_INTERNAL, "stream creation failed"));
-  for (cudaEvent_t* ev : {&g->ev_start, &g->ev_h2d, &g->ev_hash, &g->ev_exch, &g->ev_end})
+  for (cudaEvent_t* ev : {&g->ev_start, &g->ev_h2d, &g->ev_hash, &g->ev_exch, &g->ev_end, &g->ev_xfer0, &g->ev_xfer1})
     if (cudaEventCreate(ev) != cudaSuccess) return fail(set_error(TCX_INTERNAL, "event creation failed"));
   if (cudaMallocHost(&g->h_root, 256) != cudaSuccess) return fail(set_error(TCX_INTERNAL, "pinned alloc failed"));
   if (world > 1) {
@@ -571,7 +596,7 @@ extern "C" tcx_status tcx_group_join(const char* group_id, int world, int rank, 
 extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   if (g == nullptr) return TCX_OK;
   cudaSetDevice(g->device);
-  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm, g->s_pack})
+  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm, g->s_pack, g->s_local})
     if (s) cudaStreamSynchronize(s);
   if (g->comm) {
     ncclCommFinalize(g->comm);
@@ -601,9 +626,10 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   if (g->h_jobs) cudaFreeHost(g->h_jobs);
   for (auto* v : {&g->slab_events, &g->packed_events, &g->sent_events})
     for (cudaEvent_t e : *v) cudaEventDestroy(e);
-  for (cudaEvent_t e : {g->ev_start, g->ev_h2d, g->ev_hash, g->ev_exch, g->ev_end})
+  for (cudaEvent_t e : {g->ev_start, g->ev_h2d, g->ev_hash, g->ev_exch, g->ev_end, g->ev_xfer0, g->ev_xfer1})
     if (e) cudaEventDestroy(e);
-  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm, g->s_pack})
+  if (g->ev_local) cudaEventDestroy(g->ev_local);
+  for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm, g->s_pack, g->s_local})
     if (s) cudaStreamDestroy(s);
   delete g;
   return TCX_OK;
@@ -843,6 +869,74 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
     perm_bytes = std::max(perm_bytes, bytes);
   }
 
+  // --- push / NCCL split ----------------------------------------------------
+  // With the push exchange, a share of every (sender, receiver) pair's pieces
+  // (plan->push_nccl_permille of its bytes, whole pieces in view order) can go
+  // over NCCL send/recv while the rest is copied by the copy engines: the copy
+  // engines of a GPU top out near 390 GB/s in an all-to-all among 4 GPUs, and
+  // NCCL's SM-driven transfer adds its own bandwidth beside them. Every rank
+  // derives the same split from the same plan; the NCCL part is planned as a
+  // load of only those pieces.
+  const bool push = world > 1 && (plan->flags & TCX_LOAD_PEER_PUSH) != 0;
+  const uint64_t nccl_share = push ? std::min<uint64_t>(plan->push_nccl_permille, 1000) : 0;
+  const std::vector<uint64_t> recv_counts_all(recv_counts.begin(), recv_counts.end());
+  std::vector<tcx_copy_job> ce_jobs;  // hybrid: this rank's copy-engine pieces, grouped by receiver
+  std::vector<uint64_t> ce_off(world + 1, 0);
+  std::vector<tcx_copy_job> nccl_jobs;
+  std::vector<uint64_t> nccl_job_off(world + 1, 0);
+  if (nccl_share > 0) {
+    std::vector<tcx_copy_job> pieces;
+    for (int r = 0; r < world; ++r) {
+      nccl_job_off[r] = nccl_jobs.size();
+      ce_off[r] = ce_jobs.size();
+      for (int p = 0; p < world; ++p) {
+        if (p == r) continue;
+        pieces.clear();
+        clip_jobs(plan->jobs + plan->job_offsets[r], plan->job_offsets[r + 1] - plan->job_offsets[r], b[p], b[p + 1],
+                  pieces);
+        uint64_t total = 0;
+        for (const auto& j : pieces) total += j.rows * j.row_bytes;
+        const uint64_t want = (total * nccl_share + 999) / 1000;
+        uint64_t acc = 0;
+        for (auto j : pieces) {
+          if (acc < want) {
+            acc += j.rows * j.row_bytes;
+            nccl_jobs.push_back(j);
+          } else if (p == rank) {
+            j.src_off -= lo;
+            ce_jobs.push_back(j);
+          }
+        }
+      }
+    }
+    nccl_job_off[world] = nccl_jobs.size();
+    ce_off[world] = ce_jobs.size();
+    tcx_load_plan nplan = *plan;
+    nplan.jobs = nccl_jobs.data();
+    nplan.job_offsets = nccl_job_off.data();
+    nplan.permutes = nullptr;
+    nplan.n_permutes = 0;
+    nplan.flags = 0;
+    const uint64_t ncap = tcx_plan_exchange_capacity(&nplan, world);
+    std::vector<tcx_copy_job> npack(ncap), nlocal(ncap), nscatter(ncap);
+    std::vector<uint64_t> nsend(world + 1), nrecv_off(world + 1), nrecv_counts(world), nrecv_view(world), ngaps(2 * ncap);
+    std::vector<uint8_t> ndirect(world);
+    tcx_exchange_plan nxp{npack.data(), 0, nlocal.data(), 0, nscatter.data(), 0, nsend.data(), nrecv_off.data(),
+                          nrecv_counts.data(), nrecv_view.data(), ndirect.data(), ngaps.data(), 0};
+    if ((st = tcx_plan_exchange(&nplan, world, rank, &nxp)) != TCX_OK) return st;
+    // The NCCL rounds below are built from the split's plan; this rank's own
+    // pieces and the view's gaps stay those of the full plan.
+    pack.swap(npack);
+    scatter.swap(nscatter);
+    send_off.swap(nsend);
+    recv_off.swap(nrecv_off);
+    recv_counts.swap(nrecv_counts);
+    recv_view.swap(nrecv_view);
+    direct.swap(ndirect);
+    xp.n_pack = nxp.n_pack;
+    xp.n_scatter = nxp.n_scatter;
+  }
+
   // --- exchange rounds ------------------------------------------------------
   // Each (sender, receiver) pair's bytes form one stream of send_off/recv_counts
   // bytes, moved in rounds of at most W bytes. Both sides cut the stream at the
@@ -899,11 +993,14 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
 
   // Push exchange: this rank copies each peer's view pieces from its staged range
   // straight into the peer's view over NVLink (no pack or receive buffers).
-  const bool push = world > 1 && (plan->flags & TCX_LOAD_PEER_PUSH) != 0;
   std::vector<tcx_copy_job> push_jobs;
   std::vector<uint64_t> push_off(world + 1, 0);
   uint64_t push_bytes = 0;
-  if (push) {
+  if (push && nccl_share > 0) {
+    push_jobs = ce_jobs;
+    push_off = ce_off;
+    for (const auto& j : push_jobs) push_bytes += j.rows * j.row_bytes;
+  } else if (push) {
     rounds = 0;
     round_pack.clear();
     round_scatter.clear();
@@ -1127,15 +1224,34 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
   if ((plan->flags & TCX_LOAD_TARGETS) == 0)
     for (uint64_t k = 0; k < xp.n_gaps; ++k)
       TCX_CUDA_TRY(cudaMemsetAsync(view + gaps[2 * k], 0, gaps[2 * k + 1], g->s_comm));
-  if (!local_kept.empty() &&
-      (st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), g->s_comm,
-                            load_copy_ctas(n_mine))) != TCX_OK)
-    return st;
+  // This rank's own view pieces: at N > 1 on their own stream, so that they are
+  // copied while the exchange (push copies or NCCL rounds) runs; the permutes and
+  // the view hash below wait for them.
+  cudaStream_t s_loc = world > 1 ? g->s_local : g->s_comm;
+  if (world > 1) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_local, g->ev_exch, 0));
+  if (!local_kept.empty() && world > 1 && local_copy_on_copy_engines()) {
+    for (const tcx_copy_job& j : local_kept) {
+      if (j.rows == 0 || j.row_bytes == 0) continue;
+      if (j.rows == 1)
+        TCX_CUDA_TRY(cudaMemcpyAsync(view + j.dst_off, stage + j.src_off, j.row_bytes, cudaMemcpyDeviceToDevice, s_loc));
+      else
+        TCX_CUDA_TRY(cudaMemcpy2DAsync(view + j.dst_off, j.dst_pitch, stage + j.src_off, j.src_pitch, j.row_bytes,
+                                       j.rows, cudaMemcpyDeviceToDevice, s_loc));
+    }
+  } else if (!local_kept.empty()) {
+    uint64_t local_bytes = 0;
+    for (const tcx_copy_job& j : local_kept) local_bytes += j.rows * j.row_bytes;
+    if ((st = launch_copy_jobs(stage, view, dj + o_local, local_kept.size(), prefix_for(local_kept.size()), s_loc,
+                               load_copy_ctas(n_mine, local_bytes, L))) != TCX_OK)
+      return st;
+  }
+  if (world > 1) TCX_CUDA_TRY(cudaEventRecord(g->ev_local, g->s_local));
   uint64_t sent = 0, received = 0;
   if (push) {
     // Every rank's view is ready to be written (its gaps cleared, its earlier loads done).
     if ((st = nccl_barrier(g, deadline)) != TCX_OK) return st;
     TCX_CUDA_TRY(cudaEventRecord(g->ev_push, g->s_comm));
+    TCX_CUDA_TRY(cudaEventRecord(g->ev_xfer0, g->s_comm));
     // The pushes run on the copy engines, one stream per peer: no SM time is
     // taken from the leaf hash that is still running, and the peers' transfers
     // proceed side by side. A job is one 2-D copy (rows at the source and
@@ -1155,14 +1271,9 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
                                          j.rows, cudaMemcpyDeviceToDevice, sp));
       }
       TCX_CUDA_TRY(cudaEventRecord(g->peer_done[p], sp));
-      TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->peer_done[p], 0));
     }
-    // Every peer has finished writing into this rank's view.
-    if ((st = nccl_barrier(g, deadline)) != TCX_OK) return st;
-    sent = push_bytes;
-    for (int p = 0; p < world; ++p)
-      if (p != rank) received += recv_counts[p];
   }
+  if (rounds && !push) TCX_CUDA_TRY(cudaEventRecord(g->ev_xfer0, g->s_comm));
   for (uint64_t k = 0; k < rounds; ++k) {
     const uint64_t buf = k % 2;
     // pack round k on the pack stream once round k-2 (same buffer) has been sent
@@ -1194,11 +1305,25 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
     }
     if ((st = nccl_check(g, ncclGroupEnd(), deadline, "exchange")) != TCX_OK) return st;
     TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
+    if (k + 1 == rounds && !push) TCX_CUDA_TRY(cudaEventRecord(g->ev_xfer1, g->s_comm));
     const uint64_t ns = scat_off[k + 1] - scat_off[k];
     if (ns && (st = launch_copy_jobs(g->recv.p, view, dj + o_scatter + scat_off[k], ns,
                                      prefix_for(ns), g->s_comm)) != TCX_OK)
       return st;
   }
+  if (push) {
+    for (int p = 0; p < world; ++p)
+      if (p != rank && push_off[p + 1] != push_off[p])
+        TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->peer_done[p], 0));
+    TCX_CUDA_TRY(cudaEventRecord(g->ev_xfer1, g->s_comm));  // this rank's pushes (and NCCL rounds) are done
+    // Every peer has finished writing into this rank's view.
+    if ((st = nccl_barrier(g, deadline)) != TCX_OK) return st;
+    sent += push_bytes;
+    received = 0;
+    for (int p = 0; p < world; ++p)
+      if (p != rank) received += recv_counts_all[p];
+  }
+  if (ag_rounds) TCX_CUDA_TRY(cudaEventRecord(g->ev_xfer0, g->s_comm));
   for (uint64_t k = 0; k < ag_rounds; ++k) {
     // The window slots of round k were last read by the extraction of round k-2.
     if (k >= 2) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[k - 2], 0));
@@ -1215,14 +1340,16 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
     }
     if ((st = nccl_check(g, ncclGroupEnd(), deadline, "exchange")) != TCX_OK) return st;
     TCX_CUDA_TRY(cudaEventRecord(g->sent_events[k], g->s_comm));
+    if (k + 1 == ag_rounds) TCX_CUDA_TRY(cudaEventRecord(g->ev_xfer1, g->s_comm));
     TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_pack, g->sent_events[k], 0));
     const uint64_t ne = ag_off[k + 1] - ag_off[k];
     if (ne && (st = launch_copy_jobs(g->recv.p, view, dj + o_ag + ag_off[k], ne, prefix_for(ne), g->s_pack,
-                                     load_copy_ctas(n_mine))) != TCX_OK)
+                                     load_copy_ctas(n_mine, 0, L))) != TCX_OK)
       return st;
     TCX_CUDA_TRY(cudaEventRecord(g->packed_events[k], g->s_pack));
   }
   if (ag_rounds) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->packed_events[ag_rounds - 1], 0));
+  if (world > 1) TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_comm, g->ev_local, 0));
   for (uint64_t i = 0; i < plan->n_permutes; ++i) {
     tcx_permute_job pj = plan->permutes[i];
     uint64_t bytes = pj.esize;
@@ -1274,6 +1401,7 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
   out->exchange_ms = elapsed_ms(g->ev_h2d, g->ev_exch);
   out->total_ms = elapsed_ms(g->ev_start, g->ev_end);
   out->stage_read_ms = read_ms;
+  out->transfer_ms = (push || rounds || ag_rounds) ? elapsed_ms(g->ev_xfer0, g->ev_xfer1) : 0.f;
   if (view_hash) {
     encode_multihash(g->h_root + 64, out->view_multihash);
     out->view_leaf_bytes = view_leaf;

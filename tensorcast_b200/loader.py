@@ -47,7 +47,7 @@ class _Plan:
     """A tcx_load_plan with its arrays kept alive."""
 
     def __init__(self, total, leaf, bounds, rank_jobs, permutes=(), view_bytes=0, slab_bytes=0, window_bytes=0,
-                 flags=0, target_ranges=None):
+                 flags=0, target_ranges=None, push_nccl_share=0.0):
         self.bounds = np.ascontiguousarray(bounds, dtype=np.uint64)
         self.targets = None if target_ranges is None else np.ascontiguousarray(target_ranges, dtype=np.uint64).ravel()
         self.jobs, self.job_offsets = _jobs_concat(rank_jobs)
@@ -59,7 +59,8 @@ class _Plan:
             n_permutes=0 if self.perms is None else len(self.perms), view_bytes=int(view_bytes),
             slab_bytes=int(slab_bytes), window_bytes=int(window_bytes), flags=int(flags),
             target_ranges=None if self.targets is None else self.targets.ctypes.data,
-            n_targets=0 if self.targets is None else len(self.targets) // 2)
+            n_targets=0 if self.targets is None else len(self.targets) // 2,
+            push_nccl_permille=int(round(max(0.0, min(1.0, push_nccl_share)) * 1000)))
 
 
 def plan_exchange(total, leaf, bounds, rank_jobs, rank, view_bytes=0) -> dict:
@@ -181,7 +182,7 @@ class Group:
     def load(self, total, leaf, bounds, rank_jobs, *, d_stage, d_view, h_stage=None, files=None, permutes=(),
              view_bytes=None, expected_root: bytes | None = None, slab_bytes: int = 0, window_bytes: int = 0,
              view_hash: bool = False, peer_push: bool = False, target_ranges=None, all_gather: bool = False,
-             read_threads: int = 0, ring_slots: int = 0, slot_bytes: int = 0) -> dict:
+             read_threads: int = 0, ring_slots: int = 0, slot_bytes: int = 0, push_nccl_share: float = 0.0) -> dict:
         """Runs one load; returns the result fields as a dict. h_stage None and files None:
         device-resident (d_stage already holds this rank's range).
 
@@ -191,7 +192,8 @@ class Group:
         with the copies to the device and the hash (tcx_group_load_files).
 
         peer_push: exchange by copying into the peers' views over NVLink (d_view must be a
-        cudaMalloc allocation of this process, e.g. a torch CUDA tensor); all_gather: a windowed
+        cudaMalloc allocation, e.g. a torch CUDA tensor); push_nccl_share (0..1): that share of
+        every peer pair's bytes goes over NCCL send/recv beside the copy engines; all_gather: a windowed
         all-gather of every rank's staged bytes instead (every rank sees every byte); else the
         NCCL send/recv shard exchange.
         target_ranges: (offset, length) pairs of separate target tensors (TCX_LOAD_TARGETS):
@@ -201,7 +203,7 @@ class Group:
         plan = _Plan(total, leaf, bounds, rank_jobs, permutes, view_bytes, slab_bytes, window_bytes,
                      flags=(VIEW_HASH if view_hash else 0) | (PEER_PUSH if peer_push else 0) |
                      (TARGETS if target_ranges is not None else 0) | (ALLGATHER if all_gather else 0),
-                     target_ranges=target_ranges)
+                     target_ranges=target_ranges, push_nccl_share=push_nccl_share)
         res = _native.LoadResult()
         exp = None
         if expected_root is not None:
@@ -230,7 +232,7 @@ class Group:
                 "peer_recv_bytes": res.peer_recv_bytes, "h2d_ms": res.h2d_ms, "hash_ms": res.hash_ms,
                 "exchange_ms": res.exchange_ms, "total_ms": res.total_ms,
                 "view_multihash": res.view_multihash.decode(), "view_leaf_bytes": res.view_leaf_bytes,
-                "stage_read_ms": res.stage_read_ms}
+                "stage_read_ms": res.stage_read_ms, "transfer_ms": res.transfer_ms}
 
     def close(self) -> None:
         if self._h:

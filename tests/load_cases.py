@@ -24,8 +24,9 @@ def llama_tensors() -> dict:
 
 
 def run_cases(group, world: int, rank: int, gather, tmpdir: str, log=print) -> int:
-    """All exchange modes (NCCL send/recv with and without windows, peer push, windowed
-    all-gather), staged from pinned memory, from files, or device-resident; then the
+    """All exchange modes (NCCL send/recv with and without windows, peer push, the push with
+    a share of every pair's bytes over NCCL, windowed all-gather), staged from pinned
+    memory, from files, or device-resident; then the
     bind-into targets case. gather(jobs) returns every rank's jobs. Returns the failures."""
     failures = 0
     llama = llama_tensors()
@@ -59,12 +60,14 @@ def run_cases(group, world: int, rank: int, gather, tmpdir: str, log=print) -> i
         d_view = torch.full((max(plan.view_bytes, 1),), 0x3C, dtype=torch.uint8, device="cuda")
         want_root = oracle.tree_root(oracle.leaf_digests(canon, leaf))
         want = oviews.materialize_view(canon, meta, slices, transpose, subset)
-        for src, window, push, ag in (("host", 0, False, False), ("device", 0, False, False),
-                                      ("device", 1000, False, False), ("host", 4096, False, False),
-                                      ("files", 0, False, False), ("host", 0, True, False),
-                                      ("device", 0, True, False), ("files", 0, True, False),
-                                      ("host", 0, False, True), ("device", 3000, False, True),
-                                      ("files", 2048, False, True)):
+        for src, window, push, ag, share in (("host", 0, False, False, 0), ("device", 0, False, False, 0),
+                                             ("device", 1000, False, False, 0), ("host", 4096, False, False, 0),
+                                             ("files", 0, False, False, 0), ("host", 0, True, False, 0),
+                                             ("device", 0, True, False, 0), ("files", 0, True, False, 0),
+                                             ("device", 0, True, False, 0.5), ("files", 2048, True, False, 0.3),
+                                             ("host", 1000, True, False, 1.0),
+                                             ("host", 0, False, True, 0), ("device", 3000, False, True, 0),
+                                             ("files", 2048, False, True, 0)):
             if src == "device":
                 d_stage[: hi - lo].copy_(torch.from_numpy(canon[lo:hi]).cuda())
             d_view.fill_(0x3C)
@@ -73,10 +76,11 @@ def run_cases(group, world: int, rank: int, gather, tmpdir: str, log=print) -> i
                              read_threads=3, ring_slots=2, slot_bytes=1 << 12,
                              permutes=plan.permutes, view_bytes=plan.view_bytes, expected_root=want_root,
                              slab_bytes=256 if src == "host" else 0, window_bytes=window, peer_push=push,
-                             all_gather=ag)
+                             all_gather=ag, push_nccl_share=share)
             got = d_view.cpu().numpy()[: plan.view_bytes]
             if res["root"] != want_root or got.size != want.size or not (got == want).all():
-                log(f"rank {rank}: case {name} src={src} window={window} push={push} all_gather={ag} FAILED")
+                log(f"rank {rank}: case {name} src={src} window={window} push={push} share={share} "
+                    f"all_gather={ag} FAILED")
                 failures += 1
     # Separate target tensors (bind_into, TCX_LOAD_TARGETS) over the NCCL exchange:
     # the Llama TP views with every tensor in its own allocation, guard bytes around.
