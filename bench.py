@@ -720,20 +720,30 @@ def main() -> None:
         # mappings, so the views freed above are returned to their devices.
         group.close()
         torch.cuda.empty_cache()
+        def leg(name, fn):
+            # A leg that raises is recorded and the rest still run (the main line is
+            # printed in any case); device memory left by it is released first.
+            try:
+                extras[name] = fn()
+            except Exception as e:  # noqa: BLE001
+                extras[name] = {"error": f"{type(e).__name__}: {e}"[:400]}
+                log(f"{name} leg failed: {e}")
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+
         if world > 1:
-            extras["bind_into"] = bind_into_check(args, path, index, world, rank, local)
+            leg("bind_into", lambda: bind_into_check(args, path, index, world, rank, local))
             if args.model == "llama3-8b" and not args.no_c4:
-                g4 = Group.from_torch_distributed(local)
-                try:
-                    extras["c4"] = c4_leg(args, g4, world, rank, local, read_threads, args.c4_exchange)
-                finally:
-                    g4.close()
-        try:
-            extras["kv"] = kv_measure(args, world, rank, local)
-        except torch.OutOfMemoryError as e:
-            extras["kv"] = {"unavailable": f"device memory: {e}"[:300]}
+                def c4():
+                    g4 = Group.from_torch_distributed(local)
+                    try:
+                        return c4_leg(args, g4, world, rank, local, read_threads, args.c4_exchange)
+                    finally:
+                        g4.close()
+                leg("c4", c4)
+        leg("kv", lambda: kv_measure(args, world, rank, local))
         if world == 1:
-            extras["disk_hash"] = measure_disk_hash(args, min(args.steps, 5), 1)
+            leg("disk_hash", lambda: measure_disk_hash(args, min(args.steps, 5), 1))
     bad = []
     if rank == 0:
         line.update({k: v for k, v in extras.items() if v is not None})
