@@ -350,6 +350,23 @@ uint64_t tcx_plan_exchange_capacity(const tcx_load_plan* plan, int world);
 /* Host-only: the exchange schedule of `rank` in a `world`-rank load. */
 tcx_status tcx_plan_exchange(const tcx_load_plan* plan, int world, int rank, tcx_exchange_plan* out);
 
+/* Capacity of each output job array of tcx_plan_push_split. */
+uint64_t tcx_plan_push_split_capacity(const tcx_load_plan* plan, int world);
+
+/* Host-only: the split tcx_group_load makes of a push exchange with
+ * push_nccl_permille > 0 (no reference counterpart: the reference moves every
+ * peer's bytes with NCCL). For every (sender p, receiver r) pair, r's jobs clipped
+ * to p's staged range are taken in order; pieces go to NCCL until nccl_permille of
+ * the pair's bytes is reached, the rest to the copy engines. nccl_jobs receives
+ * every receiver's NCCL pieces (canonical source offsets, the receiver's view
+ * offsets; receiver r's at nccl_job_offsets[r..r+1]) -- a load plan of only those
+ * pieces gives the NCCL rounds; ce_jobs receives this rank's copy-engine pieces
+ * (source offsets relative to its staged range), receiver r's at ce_offsets[r..r+1].
+ * Every rank computes the same nccl_jobs from the same plan. */
+tcx_status tcx_plan_push_split(const tcx_load_plan* plan, int world, int rank, uint64_t nccl_permille,
+                               tcx_copy_job* nccl_jobs, uint64_t* nccl_job_offsets, tcx_copy_job* ce_jobs,
+                               uint64_t* ce_offsets, uint64_t capacity);
+
 /* Reads segments into dst (pinned or pageable host memory) with `threads`
  * parallel preads; a short read is DATA_LOSS (source_hash.cc:44-51).
  * Equivalent to tcx_read_segments_ex(segs, n, dst, threads, 0). */

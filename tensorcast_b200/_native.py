@@ -131,6 +131,9 @@ _SIGNATURES = {
     "tcx_permute": (_c.c_int, [_c.c_void_p, _c.c_void_p, _c.POINTER(PermuteJob), _c.c_void_p]),
     "tcx_plan_exchange_capacity": (_c.c_uint64, [_c.POINTER(LoadPlan), _c.c_int]),
     "tcx_plan_exchange": (_c.c_int, [_c.POINTER(LoadPlan), _c.c_int, _c.c_int, _c.POINTER(ExchangePlan)]),
+    "tcx_plan_push_split_capacity": (_c.c_uint64, [_c.POINTER(LoadPlan), _c.c_int]),
+    "tcx_plan_push_split": (_c.c_int, [_c.POINTER(LoadPlan), _c.c_int, _c.c_int, _c.c_uint64, _c.c_void_p,
+                                       _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_uint64]),
     "tcx_read_segments": (_c.c_int, [_c.POINTER(FileSegment), _c.c_uint64, _c.c_void_p, _c.c_int]),
     "tcx_read_segments_ex": (_c.c_int, [_c.POINTER(FileSegment), _c.c_uint64, _c.c_void_p, _c.c_int, _c.c_uint64]),
     "tcx_multihash_from_file_segments": (_c.c_int, [_c.POINTER(FileSegment), _c.c_uint64, _c.c_uint64, _c.c_uint64,

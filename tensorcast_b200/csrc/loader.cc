@@ -885,32 +885,14 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
   std::vector<tcx_copy_job> nccl_jobs;
   std::vector<uint64_t> nccl_job_off(world + 1, 0);
   if (nccl_share > 0) {
-    std::vector<tcx_copy_job> pieces;
-    for (int r = 0; r < world; ++r) {
-      nccl_job_off[r] = nccl_jobs.size();
-      ce_off[r] = ce_jobs.size();
-      for (int p = 0; p < world; ++p) {
-        if (p == r) continue;
-        pieces.clear();
-        clip_jobs(plan->jobs + plan->job_offsets[r], plan->job_offsets[r + 1] - plan->job_offsets[r], b[p], b[p + 1],
-                  pieces);
-        uint64_t total = 0;
-        for (const auto& j : pieces) total += j.rows * j.row_bytes;
-        const uint64_t want = (total * nccl_share + 999) / 1000;
-        uint64_t acc = 0;
-        for (auto j : pieces) {
-          if (acc < want) {
-            acc += j.rows * j.row_bytes;
-            nccl_jobs.push_back(j);
-          } else if (p == rank) {
-            j.src_off -= lo;
-            ce_jobs.push_back(j);
-          }
-        }
-      }
-    }
-    nccl_job_off[world] = nccl_jobs.size();
-    ce_off[world] = ce_jobs.size();
+    const uint64_t scap = tcx_plan_push_split_capacity(plan, world);
+    nccl_jobs.resize(scap);
+    ce_jobs.resize(scap);
+    if ((st = tcx_plan_push_split(plan, world, rank, nccl_share, nccl_jobs.data(), nccl_job_off.data(), ce_jobs.data(),
+                                  ce_off.data(), scap)) != TCX_OK)
+      return st;
+    nccl_jobs.resize(nccl_job_off[world]);
+    ce_jobs.resize(ce_off[world]);
     tcx_load_plan nplan = *plan;
     nplan.jobs = nccl_jobs.data();
     nplan.job_offsets = nccl_job_off.data();

@@ -246,3 +246,51 @@ extern "C" tcx_status tcx_plan_exchange(const tcx_load_plan* plan, int world, in
   out->n_gaps = n_gaps;
   return TCX_OK;
 }
+
+extern "C" uint64_t tcx_plan_push_split_capacity(const tcx_load_plan* plan, int world) {
+  if (plan == nullptr || plan->job_offsets == nullptr || world < 1) return 0;
+  return 3 * plan->job_offsets[world] * static_cast<uint64_t>(world) + 2;
+}
+
+extern "C" tcx_status tcx_plan_push_split(const tcx_load_plan* plan, int world, int rank, uint64_t nccl_permille,
+                                          tcx_copy_job* nccl_jobs, uint64_t* nccl_job_offsets, tcx_copy_job* ce_jobs,
+                                          uint64_t* ce_offsets, uint64_t capacity) {
+  tcx_status st = validate_plan(plan, world);
+  if (st != TCX_OK) return st;
+  if (rank < 0 || rank >= world) return set_error(TCX_INVALID_ARGUMENT, "rank out of range");
+  if (nccl_jobs == nullptr || nccl_job_offsets == nullptr || ce_jobs == nullptr || ce_offsets == nullptr)
+    return set_error(TCX_INVALID_ARGUMENT, "push split output arrays are required");
+  const uint64_t share = std::min<uint64_t>(nccl_permille, 1000);
+  const uint64_t* b = plan->stage_bounds;
+  const uint64_t* jo = plan->job_offsets;
+  const uint64_t lo = b[rank];
+  std::vector<tcx_copy_job> pieces;
+  uint64_t n_nccl = 0, n_ce = 0;
+  for (int r = 0; r < world; ++r) {
+    nccl_job_offsets[r] = n_nccl;
+    ce_offsets[r] = n_ce;
+    for (int p = 0; p < world; ++p) {
+      if (p == r) continue;
+      pieces.clear();
+      clip_jobs(plan->jobs + jo[r], jo[r + 1] - jo[r], b[p], b[p + 1], pieces);
+      uint64_t total = 0;
+      for (const auto& j : pieces) total += job_total(j);
+      const uint64_t want = (total * share + 999) / 1000;
+      uint64_t acc = 0;
+      for (auto j : pieces) {
+        if (acc < want) {
+          acc += job_total(j);
+          if (n_nccl >= capacity) return set_error(TCX_INVALID_ARGUMENT, "push split capacity too small");
+          nccl_jobs[n_nccl++] = j;
+        } else if (p == rank) {
+          j.src_off -= lo;
+          if (n_ce >= capacity) return set_error(TCX_INVALID_ARGUMENT, "push split capacity too small");
+          ce_jobs[n_ce++] = j;
+        }
+      }
+    }
+  }
+  nccl_job_offsets[world] = n_nccl;
+  ce_offsets[world] = n_ce;
+  return TCX_OK;
+}

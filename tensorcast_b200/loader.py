@@ -87,6 +87,21 @@ def plan_exchange(total, leaf, bounds, rank_jobs, rank, view_bytes=0) -> dict:
     return out
 
 
+def plan_push_split(total, leaf, bounds, rank_jobs, rank, nccl_share: float) -> dict:
+    """Host-only split of a push exchange (tcx_plan_push_split): {"nccl": every receiver's
+    NCCL pieces (list of job arrays), "ce": this rank's copy-engine pieces per receiver}."""
+    world = len(bounds) - 1
+    plan = _Plan(total, leaf, bounds, rank_jobs)
+    L = _native.lib()
+    cap = int(L.tcx_plan_push_split_capacity(ctypes.byref(plan.c), world))
+    nj, ce = np.zeros(cap, JOB_DTYPE), np.zeros(cap, JOB_DTYPE)
+    noff, coff = np.zeros(world + 1, np.uint64), np.zeros(world + 1, np.uint64)
+    _native.call("tcx_plan_push_split", ctypes.byref(plan.c), world, rank, int(round(nccl_share * 1000)),
+                 nj.ctypes.data, noff.ctypes.data, ce.ctypes.data, coff.ctypes.data, cap)
+    return {"nccl": [nj[int(noff[r]):int(noff[r + 1])].copy() for r in range(world)],
+            "ce": [ce[int(coff[r]):int(coff[r + 1])].copy() for r in range(world)]}
+
+
 READ_DIRECT = 1  # TCX_READ_DIRECT
 
 

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 from oracle import views as oviews
-from tensorcast_b200.loader import plan_exchange, stage_bounds
+from tensorcast_b200.loader import plan_exchange, plan_push_split, stage_bounds
 from tensorcast_b200.views import ViewSpec, NarrowOp, TransposeOp, plan_view
 from viewtools import emulate_load, index_from_meta, random_tensors, random_view, apply_jobs, apply_permutes
 
@@ -172,3 +172,69 @@ def test_exchange_schedule_into_sparse_targets(world):
                     o, n = int(exch[r]["recv_view_off"][p]), int(exch[r]["recv_counts"][p])
                     written_outside |= bool((~covered[o:o + n]).any())
             assert not written_outside, (seed, r)
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("share", [0.0, 0.3, 0.5, 1.0])
+def test_push_split_schedule_matches_oracle(world, share):
+    """The push exchange with a share over NCCL (tcx_plan_push_split): every rank derives the
+    same NCCL pieces; executing, per rank, the full plan's local pieces and gap fill, the NCCL
+    part's schedule (tcx_plan_exchange of a plan of only the NCCL pieces) and every sender's
+    copy-engine pieces gives each rank exactly the oracle's view, and the NCCL part carries
+    at least `share` of the bytes (whole pieces)."""
+    leaf = 256
+    for seed in range(5):
+        canon, meta = oviews.canonical_bytes(random_tensors(seed * 11 + world, n=20))
+        index = index_from_meta(meta, canon.size)
+        rng = np.random.default_rng(seed + 100)
+        bounds = stage_bounds(canon.size, leaf, world)
+        views = [random_view(meta, rng) for _ in range(world)]
+        plans = [plan_view(index, v[3], v[2]) for v in views]
+        rank_jobs = [p.jobs for p in plans]
+        splits = [plan_push_split(canon.size, leaf, bounds, rank_jobs, r, share) for r in range(world)]
+        for r in range(1, world):
+            for q in range(world):
+                assert splits[r]["nccl"][q].tobytes() == splits[0]["nccl"][q].tobytes()
+        nccl_jobs = splits[0]["nccl"]
+        full = [plan_exchange(canon.size, leaf, bounds, rank_jobs, r, plans[r].view_bytes) for r in range(world)]
+        part = [plan_exchange(canon.size, leaf, bounds, nccl_jobs, r, plans[r].view_bytes) for r in range(world)]
+        views_out, sends = [], []
+        for r in range(world):
+            stage = canon[bounds[r]:bounds[r + 1]]
+            view = np.full(plans[r].view_bytes, 0xA5, np.uint8)
+            for off, ln in full[r]["gaps"]:
+                view[int(off): int(off) + int(ln)] = 0
+            apply_jobs(stage, view, full[r]["local"])
+            views_out.append(view)
+            send = np.zeros(int(part[r]["send_offsets"][-1]), np.uint8)
+            apply_jobs(stage, send, part[r]["pack"])
+            sends.append(send)
+            assert len(part[r]["local"]) == 0
+        nccl_bytes = total_bytes = 0
+        for r in range(world):
+            x = part[r]
+            recv = np.zeros(int(x["recv_offsets"][-1]), np.uint8)
+            for p in range(world):
+                if p == r:
+                    continue
+                data = sends[p][int(part[p]["send_offsets"][r]): int(part[p]["send_offsets"][r + 1])]
+                nccl_bytes += data.size
+                if x["direct"][p]:
+                    views_out[r][int(x["recv_view_off"][p]): int(x["recv_view_off"][p]) + data.size] = data
+                else:
+                    recv[int(x["recv_offsets"][p]): int(x["recv_offsets"][p]) + data.size] = data
+                # sender p's copy-engine pieces into r's view
+                apply_jobs(canon[bounds[p]:bounds[p + 1]], views_out[r], splits[p]["ce"][r])
+                total_bytes += int(full[r]["recv_counts"][p])
+            apply_jobs(recv, views_out[r], x["scatter"])
+            apply_permutes(views_out[r], plans[r].permutes)
+        for r in range(world):
+            slices, transpose, subset, _ = views[r]
+            want = oviews.materialize_view(canon, meta, slices, transpose, subset)
+            assert views_out[r].size == want.size and (views_out[r] == want).all(), (seed, r)
+        if share == 0.0:
+            assert nccl_bytes == 0
+        elif share == 1.0:
+            assert nccl_bytes == total_bytes
+        else:  # whole pieces in order until the share is reached: at least the share of every pair
+            assert share * total_bytes <= nccl_bytes <= total_bytes
