@@ -176,21 +176,25 @@ __global__ void __launch_bounds__(kLeafThreads) sha256_leaf_kernel(const uint8_t
 
 // ---------------------------------------------------------------------------
 // Warp-specialised leaf kernel (16-byte aligned leaves only).
-// CTA = kWsPairs consumer warps (warps 0..P-1) + kWsPairs producer warps
-// (warps P..2P-1); producer warp P+c feeds consumer warp c, lane j <-> chain j.
+// CTA = P consumer warps (warps 0..P-1) + P producer warps (warps P..2P-1);
+// producer warp P+c feeds consumer warp c, lane j <-> chain j.
 // Shared ring per pair: kWsStages stages x kWsBlocks blocks x 64 words x 32 lanes,
 // laid out [stage][block][t/4][lane][t%4] so that each lane moves 16 bytes per
 // access and a warp touches 512 contiguous bytes (no bank conflicts).
 // ---------------------------------------------------------------------------
-constexpr int kWsPairs = 2;
 constexpr int kWsStages = 2;
-constexpr int kWsThreads = 64 * kWsPairs;
 constexpr int kWsBlockWords = 64 * 32;
-// Blocks per stage: 4 when the grid is one wave (one CTA per SM, 128 KiB of
-// ring; measured 1.7% faster per block on the 3830-chain Llama-3-8B load than
-// 2, fewer ring hand-offs), else 2 (64 KiB, so three CTAs fit on an SM).
-constexpr size_t ws_smem_bytes(int blocks) {
-  return static_cast<size_t>(kWsPairs) * kWsStages * blocks * kWsBlockWords * 4;
+// Layouts (pairs per CTA, blocks per stage), by chains n:
+//  * <2, 4> while the grid is one wave (n <= 64 per SM): warps 0-3 of the CTA sit
+//    on SMSPs 0-3, so each consumer has an SMSP to itself; 4 blocks per stage
+//    (128 KiB of ring) measured 1.7% faster per block than 2 on the 3830-chain
+//    Llama-3-8B load (fewer ring hand-offs);
+//  * <4, 2> for one more wave's worth of chains (n <= 128 per SM): one CTA per
+//    SM whose four consumers and four producers share the four SMSPs one each,
+//    instead of a second <2, *> CTA stacking two consumers on SMSPs 0 and 1;
+//  * <2, 2> beyond that (64 KiB, three CTAs per SM).
+constexpr size_t ws_smem_bytes(int pairs, int blocks) {
+  return static_cast<size_t>(pairs) * kWsStages * blocks * kWsBlockWords * 4;
 }
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
@@ -278,12 +282,13 @@ __device__ __forceinline__ void ws_consume_block(uint32_t s[8], const uint4* src
   }
 }
 
-template <int kWsBlocks>
-__global__ void __launch_bounds__(kWsThreads, 1) sha256_leaf_ws_kernel(const uint8_t* __restrict__ src,
-                                                                       LeafGeom geom, uint32_t n_leaves,
-                                                                       uint64_t seg_off, uint64_t seg_len,
-                                                                       uint32_t* __restrict__ states,
-                                                                       uint8_t* __restrict__ digests) {
+template <int kWsPairs, int kWsBlocks>
+__global__ void __launch_bounds__(64 * kWsPairs, 1) sha256_leaf_ws_kernel(const uint8_t* __restrict__ src,
+                                                                          LeafGeom geom, uint32_t n_leaves,
+                                                                          uint64_t seg_off, uint64_t seg_len,
+                                                                          uint32_t* __restrict__ states,
+                                                                          uint8_t* __restrict__ digests) {
+  static_assert(kWsPairs * 2 * kWsStages <= 16, "named barriers 0..15");
   constexpr int kWsStageWords = kWsBlocks * kWsBlockWords;
   extern __shared__ uint4 ws_smem[];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -294,7 +299,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) sha256_leaf_ws_kernel(const uin
   const uint32_t max_nb = __reduce_max_sync(0xffffffffu, ps.active ? ps.nb : 0u);
   const uint32_t n_stages = (max_nb + kWsBlocks - 1) / kWsBlocks;
   uint4* ring = ws_smem + static_cast<size_t>(pair) * kWsStages * (kWsStageWords / 4);
-  const uint32_t bar_full = 1u + pair * 2u * kWsStages;
+  // Named barriers pair*4 + {0, 1} (stage full) and + {2, 3} (stage empty); the
+  // kernel never uses barrier 0 otherwise (no __syncthreads).
+  const uint32_t bar_full = pair * 2u * kWsStages;
   const uint32_t bar_empty = bar_full + kWsStages;
 
   if (producer) {
@@ -556,20 +563,31 @@ static tcx_status launch_leaf_kernels(const uint8_t* src, const LeafGeom& geom, 
     int dev = 0;
     TCX_CUDA_TRY(cudaGetDevice(&dev));
     if (configured_device != dev) {
-      TCX_CUDA_TRY(cudaFuncSetAttribute(sha256_leaf_ws_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(ws_smem_bytes(2))));
-      TCX_CUDA_TRY(cudaFuncSetAttribute(sha256_leaf_ws_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(ws_smem_bytes(4))));
+      TCX_CUDA_TRY(cudaFuncSetAttribute(sha256_leaf_ws_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(ws_smem_bytes(2, 2))));
+      TCX_CUDA_TRY(cudaFuncSetAttribute(sha256_leaf_ws_kernel<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(ws_smem_bytes(2, 4))));
+      TCX_CUDA_TRY(cudaFuncSetAttribute(sha256_leaf_ws_kernel<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(ws_smem_bytes(4, 2))));
       configured_device = dev;
     }
-    const uint64_t ctas = div_up(n, 32u * kWsPairs);
-    const dim3 grid(static_cast<unsigned>(ctas));
-    if (ctas <= static_cast<uint64_t>(sm_count()))
-      sha256_leaf_ws_kernel<4><<<grid, kWsThreads, ws_smem_bytes(4), stream>>>(src, geom, n, seg_off, seg_len, states,
-                                                                               out);
-    else
-      sha256_leaf_ws_kernel<2><<<grid, kWsThreads, ws_smem_bytes(2), stream>>>(src, geom, n, seg_off, seg_len, states,
-                                                                               out);
+    const uint64_t sms = static_cast<uint64_t>(sm_count());
+    int layout = n <= sms * 64 ? 0 : (n <= sms * 128 ? 1 : 2);
+    // TCX_WS_LAYOUT=0|1|2 forces a layout (measurement knob).
+    if (const char* v = std::getenv("TCX_WS_LAYOUT")) layout = std::atoi(v) % 3;
+    if (layout == 0) {
+      const dim3 grid(static_cast<unsigned>(div_up(n, 64u)));
+      sha256_leaf_ws_kernel<2, 4><<<grid, 128, ws_smem_bytes(2, 4), stream>>>(src, geom, n, seg_off, seg_len, states,
+                                                                              out);
+    } else if (layout == 1) {
+      const dim3 grid(static_cast<unsigned>(div_up(n, 128u)));
+      sha256_leaf_ws_kernel<4, 2><<<grid, 256, ws_smem_bytes(4, 2), stream>>>(src, geom, n, seg_off, seg_len, states,
+                                                                              out);
+    } else {
+      const dim3 grid(static_cast<unsigned>(div_up(n, 64u)));
+      sha256_leaf_ws_kernel<2, 2><<<grid, 128, ws_smem_bytes(2, 2), stream>>>(src, geom, n, seg_off, seg_len, states,
+                                                                              out);
+    }
     note_launches(1);
   } else if (vec) {
     const dim3 grid(static_cast<unsigned>(div_up(n, kLeafThreads)));
@@ -666,8 +684,9 @@ tcx_status preload_hash_kernels() {
   cudaFuncAttributes attr;
   TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_kernel<true>));
   TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_kernel<false>));
-  TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_ws_kernel<2>));
-  TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_ws_kernel<4>));
+  TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_ws_kernel<2, 2>));
+  TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_ws_kernel<2, 4>));
+  TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, sha256_leaf_ws_kernel<4, 2>));
   TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, merkle_level_kernel));
   TCX_CUDA_TRY(cudaFuncGetAttributes(&attr, merkle_finish_kernel));
   TCX_CUDA_TRY(cudaFuncSetAttribute(merkle_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

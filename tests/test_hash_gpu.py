@@ -126,3 +126,25 @@ def test_canonical_leaf_digests_skip_partial_leaves(cuda_device):
     got = tcx.hashing.compute_canonical_leaf_digests(to_dev(a), [3, 0, 9, 10, 11], 4096)
     want = oracle.leaf_digests(a, 4096)
     assert got == [want[3].tobytes(), want[0].tobytes(), want[9].tobytes()]  # 10 is partial, 11 beyond
+
+
+@pytest.mark.parametrize("layout", ["0", "1", "2"])
+def test_warp_specialised_layouts_bit_exact(cuda_device, layout, monkeypatch):
+    """Every CTA layout of the warp-specialised kernel (2 pairs x 4 blocks, 4 pairs x 2
+    blocks, 2 pairs x 2 blocks per stage), forced, on chain counts below, inside and above
+    one wave, single pass and streamed passes: digests equal to the oracle's."""
+    monkeypatch.setenv("TCX_HASH_KERNEL", "ws")
+    monkeypatch.setenv("TCX_WS_LAYOUT", layout)
+    for size, leaf in ((1000, 64), ((10 << 20) + 100, 1024), (64 << 20, 4096), ((80 << 20) + 4000, 2048)):
+        a = seeded(size + int(layout), size)
+        d = to_dev(a)
+        want = oracle.leaf_digests(a, leaf, openssl=True, threads=8)
+        assert (tcx.sha256_leaves(d, leaf).cpu().numpy() == want).all(), (size, leaf)
+        n = (size + leaf - 1) // leaf
+        digests = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+        states = torch.empty((n, 32), dtype=torch.uint8, device="cuda")
+        seg = max(64, (leaf // 3) // 64 * 64)
+        for off in range(0, leaf, seg):
+            _native.call("tcx_sha256_leaves_pass", d.data_ptr(), size, leaf, off, seg, states.data_ptr(),
+                         digests.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
+        assert (digests.cpu().numpy() == want).all(), (size, leaf, "streamed")
