@@ -189,9 +189,11 @@ constexpr int kWsBlockWords = 64 * 32;
 //    on SMSPs 0-3, so each consumer has an SMSP to itself; 4 blocks per stage
 //    (128 KiB of ring) measured 1.7% faster per block than 2 on the 3830-chain
 //    Llama-3-8B load (fewer ring hand-offs);
-//  * <4, 2> for one more wave's worth of chains (n <= 128 per SM): one CTA per
-//    SM whose four consumers and four producers share the four SMSPs one each,
-//    instead of a second <2, *> CTA stacking two consumers on SMSPs 0 and 1;
+//  * <4, 2> for n <= 96 per SM: one CTA per SM whose four consumers and four
+//    producers share the four SMSPs one each, instead of a second <2, *> CTA
+//    stacking two consumers on SMSPs 0 and 1. Measured on B200 (4 MiB leaves):
+//    10240 chains 102.6 ms against 109.1 ms for <2, 2>; at 17920 chains it lost
+//    (136.8 against 125.6 ms), so it stops at 96 chains per SM;
 //  * <2, 2> beyond that (64 KiB, three CTAs per SM).
 constexpr size_t ws_smem_bytes(int pairs, int blocks) {
   return static_cast<size_t>(pairs) * kWsStages * blocks * kWsBlockWords * 4;
@@ -572,7 +574,7 @@ static tcx_status launch_leaf_kernels(const uint8_t* src, const LeafGeom& geom, 
       configured_device = dev;
     }
     const uint64_t sms = static_cast<uint64_t>(sm_count());
-    int layout = n <= sms * 64 ? 0 : (n <= sms * 128 ? 1 : 2);
+    int layout = n <= sms * 64 ? 0 : (n <= sms * 96 ? 1 : 2);
     // TCX_WS_LAYOUT=0|1|2 forces a layout (measurement knob).
     if (const char* v = std::getenv("TCX_WS_LAYOUT")) layout = std::atoi(v) % 3;
     if (layout == 0) {
