@@ -62,6 +62,10 @@ def parse_args():
                     help="N>1 shard exchange: push over peer memory (copy-engine copies into the peers' views "
                          "over NVLink) or NCCL send/recv of packed windows; auto = push; allgather = windowed "
                          "broadcast of every rank's staged bytes to all ranks (every rank sees every byte)")
+    ap.add_argument("--push-nccl-share", default="auto",
+                    help="with the push exchange, the share (0..1) of every pair's bytes sent by NCCL "
+                         "send/recv beside the copy-engine copies; auto = the share measured best for the "
+                         "number of ranks")
     ap.add_argument("--stage", choices=["mapped", "pinned"], default="pinned",
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
                          "(no second host copy), or a pinned copy read with parallel preads")
@@ -83,6 +87,18 @@ def exchange_mode(args) -> str:
     # auto: the copy-engine push for both artifacts (with the local extraction on its own
     # stream it measured faster than NCCL send/recv on the 70B TP-2 load: 127 against 154 ms)
     return "push" if args.exchange == "auto" else args.exchange
+
+
+# Share of every pair's bytes that the push exchange sends over NCCL, by number of ranks.
+# At 2 ranks the copy engines alone already deliver about the peer-copy rate (a 20 % NCCL
+# share measured 48.5 against 47.9 ms of transfer on the 70B TP-2 load).
+AUTO_PUSH_NCCL_SHARE = {2: 0.0}
+
+
+def push_share(args, world: int) -> float:
+    if args.push_nccl_share != "auto":
+        return min(1.0, max(0.0, float(args.push_nccl_share)))
+    return AUTO_PUSH_NCCL_SHARE.get(world, 0.0)
 
 
 def _size(x: str) -> int:
@@ -495,6 +511,7 @@ def main() -> None:
                           files=files_mine if from_files else None, read_threads=read_threads,
                           permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected,
                           peer_push=exchange_mode(args) == "push" and world > 1,
+                          push_nccl_share=push_share(args, world) if exchange_mode(args) == "push" else 0.0,
                           all_gather=exchange_mode(args) == "allgather" and world > 1)
 
     def max_over_ranks(x: float) -> float:
@@ -659,8 +676,9 @@ def main() -> None:
             "roofline": hk,
             "e2e": {"value": round(T / file_ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(file_ms, 3),
                     "from": f"the safetensors file in tmpfs (page-cache resident): {read_threads} reader threads per "
-                            "rank pread into a ring of pinned slots, H2D, hash, exchange, view, 32-byte root read "
-                            "back, all inside each step (tcx_group_load_files)",
+                            "rank pread leaf pieces into small pinned buffers and queue each group's H2D copy at "
+                            "once; streamed hash, exchange, view, 32-byte root read back, all inside each step "
+                            "(tcx_group_load_files)",
                     "h2d_bytes_per_step": T, "d2h_bytes_per_step": 32 * world,
                     "stage_read_ms": round(file_read_ms, 3), "h2d_ms": round(file_h2d_ms, 3),
                     "wall_ms_per_step": round(file_wall, 3), "gpu_launches": int(file_launches),
@@ -704,7 +722,7 @@ def main() -> None:
             line["reference_gpu_kernel"] = ref_gpu
         if world > 1:
             # The shard exchange of the device-resident steps (it runs beside the hash).
-            line["exchange"] = exchange_summary(exchange_mode(args), peer, exch_ms, xfer_ms)
+            line["exchange"] = exchange_summary(exchange_mode(args), peer, exch_ms, xfer_ms, push_share(args, world))
 
     # Extra legs (driver-visible evidence of the other benchmark rows), after the main
     # workload's buffers are released: paged KV (config 5) on every N, the collective
@@ -984,12 +1002,14 @@ def verify_view_full(path, index, plan, d_view, world, rank, transposed=None):
     return all(r[0] for r in res), sum(r[1] for r in res), len(res)
 
 
-def exchange_summary(mode: str, recv: float, phase_ms: float, xfer_ms: float) -> dict:
+def exchange_summary(mode: str, recv: float, phase_ms: float, xfer_ms: float, nccl_share: float = 0.0) -> dict:
     """The shard exchange of the device-resident steps, per rank: bytes received over the
     transfer itself (pushes or NCCL rounds, device events) as a fraction of NVLink 5 (900 GB/s
     per direction) and of the measured 770 GB/s peer copy; the phase also holds the local
     extraction and runs beside the leaf hash."""
     gbs = recv / xfer_ms / 1e6 if xfer_ms > 0 else 0.0
+    if mode == "push" and nccl_share > 0:
+        mode = f"push + {nccl_share:g} of each pair's bytes over NCCL"
     return {"mode": mode, "recv_bytes_per_rank": int(recv), "transfer_ms": round(xfer_ms, 3),
             "gbs_per_rank": round(gbs, 1), "frac_of_nvlink_900": round(gbs / 900.0, 4),
             "frac_of_measured_peer_copy_770": round(gbs / 770.0, 4), "exchange_and_view_ms": round(phase_ms, 3),
@@ -1063,7 +1083,8 @@ def c4_leg(args, group, world: int, rank: int, local: int, read_threads: int, ex
         return group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view,
                           files=files if from_files else None, read_threads=read_threads,
                           permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected,
-                          peer_push=exchange == "push")
+                          peer_push=exchange == "push",
+                          push_nccl_share=push_share(args, world) if exchange == "push" else 0.0)
 
     def mx(x: float) -> float:
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
@@ -1121,7 +1142,8 @@ def c4_leg(args, group, world: int, rank: int, local: int, read_threads: int, ex
             "e2e": {"value": round(T / file_ms / 1e6, 2), "ms_per_step": round(file_ms, 3),
                     "stage_read_ms": round(read_ms, 3), "steps": 2, "warmup": 1,
                     "from": "the file in tmpfs, tcx_group_load_files on every rank"},
-            "exchange": exchange_summary(exchange, recv, exch_ms, xfer_ms),
+            "exchange": exchange_summary(exchange, recv, exch_ms, xfer_ms,
+                                         push_share(args, world) if exchange == "push" else 0.0),
             "parity": {"root_matches_cpu_oracle": bool(mn[1].item() > 0), "view_full_ok": bool(mn[0].item() > 0),
                        "view_bytes_checked": int(agg[2].item()), "view_tensors_checked": int(agg[3].item()),
                        "multihash": first["multihash"]},

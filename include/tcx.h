@@ -498,19 +498,26 @@ typedef struct tcx_file_stage {
                                        are zero (the canonical space's alignment pads) */
   uint64_t n_segments;
   int read_threads;                 /* host reader threads (0: the CPUs the caller may run on, <= 32) */
-  int ring_slots;                   /* pinned slabs read ahead (0: 4) */
-  uint64_t slot_bytes;              /* pinned bytes per slab when plan->slab_bytes is 0 (0: 512 MiB) */
+  int ring_slots;                   /* slab staging: pinned slabs read ahead (0: 4) */
+  uint64_t slot_bytes;              /* slab staging: pinned bytes per slab when plan->slab_bytes is 0
+                                       (0: 512 MiB) */
 } tcx_file_stage;
 
-/* tcx_group_load with the staged range read from files inside the call: the
- * group's reader threads pread slab j (bytes [j*S, (j+1)*S) of every leaf of the
- * range) into pinned slot j % ring_slots while earlier slabs are copied to
- * d_stage and hashed, so reads, host-to-device copies and the streamed SHA-256
- * passes overlap (the reference's read -> pinned -> H2D chunk loop with its
- * two-deep ChunkPrefetcher, collective_disk_loader.cc:2277-2383, 5538-5816).
- * The ring and the threads stay with the group for later loads. A file that
- * cannot be opened is NOT_FOUND, a short read DATA_LOSS; total_ms then covers
- * the reads as well. */
+/* tcx_group_load with the staged range read from files inside the call, so
+ * reads, host-to-device copies and the streamed SHA-256 passes overlap (the
+ * reference's read -> pinned -> H2D chunk loop with its two-deep
+ * ChunkPrefetcher, collective_disk_loader.cc:2277-2383, 5538-5816). Slab j is
+ * bytes [j*S, (j+1)*S) of every leaf of the range, and its hash pass runs once
+ * it is on the device.
+ *  - Leaves of at least two pieces (plan->slab_bytes 0): piece staging. S is a
+ *    piece of up to 256 KiB and at most half a leaf; a reader thread preads the pieces of slab j of a few
+ *    consecutive leaves (about 4 MiB) into one of its two pinned buffers and at
+ *    once queues their 2-D copy on its own stream.
+ *  - Otherwise (or with the environment variable TCX_STAGE=slabs): the readers
+ *    pread slab j into pinned slot j % ring_slots, copied with one 2-D copy.
+ * The pinned buffers and the threads stay with the group for later loads. A
+ * file that cannot be opened is NOT_FOUND, a short read DATA_LOSS; total_ms
+ * then covers the reads as well. */
 tcx_status tcx_group_load_files(tcx_group* g, const tcx_load_plan* plan, const tcx_file_stage* files, void* d_stage,
                                 void* d_view, const uint8_t* expected_root, tcx_load_result* out, void* stream);
 

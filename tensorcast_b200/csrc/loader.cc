@@ -59,6 +59,45 @@ constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchang
 constexpr uint64_t kDefaultSlotBytes = 512ull << 20;  // pinned bytes per slab when staging from files
 constexpr uint64_t kDefaultRingSlots = 4;            // slabs read ahead when staging from files
 
+// Piece staging from files (the pieces of a few leaves copied to the device as
+// soon as they are read): bytes per leaf piece, bytes per copy, and pinned
+// buffers per reader thread. It is used for leaves of at least two pieces;
+// TCX_STAGE=slabs selects the slab ring instead, and TCX_STAGE_PIECE,
+// TCX_STAGE_COPY and TCX_STAGE_PIECE_BUFS override the defaults. Measured on
+// B200 (16 GB artifact of 4 MiB leaves, tmpfs, 16 readers): 47.4-50.7 GB/s from
+// the file against 41.6-42.5 GB/s with 512 MiB slab slots, where every slab is
+// written to host DRAM in full before its copy reads it back; 2 MiB or 8 MiB
+// copies, 128 or 512 KiB pieces and 3 buffers per reader measured slower.
+constexpr uint64_t kDefaultPieceBytes = 256ull << 10;
+constexpr uint64_t kDefaultPieceCopy = 4ull << 20;
+constexpr int kDefaultPieceBufs = 2;
+constexpr uint64_t kMinPieceBytes = 64ull << 10;
+
+// Piece size for leaves of `span` bytes, 0 for slab staging: a power of two,
+// at most half the leaf (so that every leaf's chain advances over several slabs).
+uint64_t piece_bytes_for(uint64_t span) {
+  const char* mode = std::getenv("TCX_STAGE");
+  if (mode != nullptr && std::strcmp(mode, "slabs") == 0) return 0;
+  uint64_t want = kDefaultPieceBytes;
+  if (const char* v = std::getenv("TCX_STAGE_PIECE")) want = std::strtoull(v, nullptr, 0);
+  uint64_t S = kMinPieceBytes;
+  while (S * 2 <= want && S * 4 <= span) S *= 2;
+  return S * 2 <= span ? S : 0;
+}
+
+// Leaves per work item: about kDefaultPieceCopy bytes per host-to-device copy
+// (TCX_STAGE_COPY overrides), at least one leaf and at most n_rows.
+uint64_t piece_rows_for(uint64_t S, uint64_t n_rows) {
+  uint64_t want = kDefaultPieceCopy;
+  if (const char* v = std::getenv("TCX_STAGE_COPY")) want = std::strtoull(v, nullptr, 0);
+  return std::max<uint64_t>(1, std::min<uint64_t>(n_rows, want / S));
+}
+
+int piece_buffers() {
+  if (const char* v = std::getenv("TCX_STAGE_PIECE_BUFS")) return std::max(1, std::min(64, std::atoi(v)));
+  return kDefaultPieceBufs;
+}
+
 // The local extraction copy of a load runs while the leaf hash is still going.
 // With fewer chains than about one consumer warp per SMSP the hash is bound by
 // each warp's own instruction issue, and a full 8-CTA-per-SM copy grid sharing
@@ -146,10 +185,17 @@ struct ReadBatch {
 // Batches are served in submission order; a thread that finds every item of the
 // oldest batch handed out moves on to the next one, so several slabs are read
 // at once.
+// Index of the pool thread that runs the current item (-1 outside a pool).
+thread_local int t_reader = -1;
+
 class ReadPool {
  public:
   explicit ReadPool(int n) {
-    for (int i = 0; i < n; ++i) threads_.emplace_back([this] { work(); });
+    for (int i = 0; i < n; ++i)
+      threads_.emplace_back([this, i] {
+        t_reader = i;
+        work();
+      });
   }
   ~ReadPool() {
     {
@@ -251,6 +297,16 @@ struct tcx_group {
   uint8_t* h_ring = nullptr;
   uint64_t h_ring_bytes = 0;
   std::unique_ptr<ReadPool> readers;
+  // Piece staging: each reader thread owns a stream and `piece_bufs` pinned
+  // buffers of `piece_bytes` (one leaf piece each), every buffer with the event of
+  // the copy that last read it; `rd_marks` join the readers' streams per slab.
+  uint8_t* h_pieces = nullptr;
+  uint64_t h_pieces_bytes = 0, piece_bytes = 0;
+  int piece_bufs = 0;
+  std::vector<cudaStream_t> rd_streams;
+  std::vector<cudaEvent_t> rd_events, rd_marks;
+  std::vector<uint8_t> rd_used;    // per buffer: a copy was queued from it
+  std::vector<uint64_t> rd_count;  // per reader: pieces read (picks the next buffer)
 };
 
 namespace {
@@ -618,7 +674,14 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   for (cudaStream_t s : g->s_peer)
     if (s) cudaStreamDestroy(s);
   g->readers.reset();  // joins the reader threads before their ring goes away
+  for (cudaStream_t s : g->rd_streams)
+    if (s) cudaStreamSynchronize(s);
   if (g->h_ring) cudaFreeHost(g->h_ring);
+  if (g->h_pieces) cudaFreeHost(g->h_pieces);
+  for (auto* v : {&g->rd_events, &g->rd_marks})
+    for (cudaEvent_t e : *v) cudaEventDestroy(e);
+  for (cudaStream_t s : g->rd_streams)
+    if (s) cudaStreamDestroy(s);
   g->ipc_records.release();
   g->barrier_word.release();
   if (g->h_ipc) cudaFreeHost(g->h_ipc);
@@ -694,11 +757,9 @@ bool read_stage_range(const FileStageCtx& c, uint64_t a, uint64_t w, uint8_t* ds
 // pinned slot j % K (row r of the slot = leaf r's piece of the slab), and as soon
 // as a slot is full its H2D and hash pass are queued; slot reuse waits for the
 // H2D of the slab that last used it. Reads of up to K slabs run ahead.
-template <class Enqueue>
-tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t mine, uint64_t L, uint64_t S, uint64_t J,
-                            uint64_t n_full, uint64_t tail, Enqueue&& enqueue_slab, Clock::time_point deadline) {
+// Checks, sorts and opens the segments of the staged range.
+tcx_status open_stage_files(const tcx_file_stage& fs, uint64_t mine, FileStageCtx* ctx) {
   if (fs.n_segments > 0 && fs.segments == nullptr) return set_error(TCX_INVALID_ARGUMENT, "segments is null");
-  auto ctx = std::make_shared<FileStageCtx>();
   ctx->segs.reserve(fs.n_segments);
   ctx->paths.reserve(fs.n_segments);
   for (uint64_t i = 0; i < fs.n_segments; ++i) {
@@ -729,6 +790,24 @@ tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t min
     }
     ctx->fds[i] = it->second;
   }
+  return TCX_OK;
+}
+
+// The group's reader pool with nt threads (kept between loads).
+void ensure_readers(tcx_group* g, int nt) {
+  if (!g->readers || g->readers->size() != nt) {
+    g->readers.reset();
+    g->readers = std::make_unique<ReadPool>(nt);
+  }
+}
+
+int reader_count(const tcx_file_stage& fs) { return fs.read_threads > 0 ? fs.read_threads : std::min(32, affinity_cpus()); }
+
+template <class Enqueue>
+tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t mine, uint64_t L, uint64_t S, uint64_t J,
+                            uint64_t n_full, uint64_t tail, Enqueue&& enqueue_slab, Clock::time_point deadline) {
+  auto ctx = std::make_shared<FileStageCtx>();
+  if (tcx_status st = open_stage_files(fs, mine, ctx.get()); st != TCX_OK) return st;
 
   const uint64_t n_rows = n_full + (tail > 0 ? 1 : 0);
   const uint64_t slot = n_rows * S;
@@ -744,11 +823,7 @@ tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t min
     }
     g->h_ring_bytes = K * slot;
   }
-  const int nt = fs.read_threads > 0 ? fs.read_threads : std::min(32, affinity_cpus());
-  if (!g->readers || g->readers->size() != nt) {
-    g->readers.reset();
-    g->readers = std::make_unique<ReadPool>(nt);
-  }
+  ensure_readers(g, reader_count(fs));
 
   std::vector<std::shared_ptr<ReadBatch>> batches(J);
   uint64_t dispatched = 0;
@@ -789,6 +864,166 @@ tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t min
     for (uint64_t k = 0; k < dispatched; ++k) batches[k]->failed = true;
     for (uint64_t k = 0; k < dispatched; ++k)
       ReadPool::wait(*batches[k], Clock::now() + std::chrono::milliseconds(g->timeout_ms));
+    cudaStreamSynchronize(g->s_copy);
+    cudaGetLastError();
+  }
+  return st;
+}
+
+// Per-reader streams, copy events and pinned piece buffers for piece staging.
+tcx_status ensure_piece_buffers(tcx_group* g, int nt, uint64_t S, int bufs) {
+  if (static_cast<int>(g->rd_streams.size()) == nt && g->piece_bufs == bufs && g->piece_bytes >= S) return TCX_OK;
+  for (cudaStream_t s : g->rd_streams) cudaStreamSynchronize(s);
+  for (auto* v : {&g->rd_events, &g->rd_marks}) {
+    for (cudaEvent_t e : *v) cudaEventDestroy(e);
+    v->clear();
+  }
+  for (cudaStream_t s : g->rd_streams) cudaStreamDestroy(s);
+  g->rd_streams.clear();
+  if (g->h_pieces) cudaFreeHost(g->h_pieces);
+  g->h_pieces = nullptr;
+  g->h_pieces_bytes = g->piece_bytes = 0;
+  g->piece_bufs = 0;
+  const uint64_t n = static_cast<uint64_t>(nt) * bufs;
+  if (cudaError_t e = cudaHostAlloc(&g->h_pieces, n * S, cudaHostAllocPortable); e != cudaSuccess) {
+    cudaGetLastError();
+    g->h_pieces = nullptr;
+    return set_errorf(TCX_RESOURCE_EXHAUSTED, "pinned piece buffers of %llu bytes: %s",
+                      static_cast<unsigned long long>(n * S), cuda_msg(e).c_str());
+  }
+  g->h_pieces_bytes = n * S;
+  for (int t = 0; t < nt; ++t) {
+    cudaStream_t s;
+    TCX_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    g->rd_streams.push_back(s);
+  }
+  if (tcx_status st = ensure_events(g->rd_events, n); st != TCX_OK) return st;
+  if (tcx_status st = ensure_events(g->rd_marks, nt); st != TCX_OK) return st;
+  g->rd_used.assign(n, 0);
+  g->rd_count.assign(nt, 0);
+  g->piece_bytes = S;
+  g->piece_bufs = bufs;
+  return TCX_OK;
+}
+
+// Waits, with a deadline, for the copy that last read a piece buffer.
+bool wait_piece_copy(cudaEvent_t e, Clock::time_point deadline, ReadBatch& b) {
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(e);
+    if (q == cudaSuccess) return true;
+    if (q != cudaErrorNotReady) {
+      cudaGetLastError();
+      b.fail(TCX_INTERNAL, "host-to-device copy of a staged piece failed: " + cuda_msg(q));
+      return false;
+    }
+    if (Clock::now() > deadline) {
+      b.fail(TCX_DEADLINE_EXCEEDED, "host-to-device copy of a staged piece timed out");
+      return false;
+    }
+    std::this_thread::yield();
+  }
+}
+
+// Streams this rank's staged range from files in leaf pieces: piece (r, j) is
+// bytes [j*S, (j+1)*S) of leaf r, and a work item is the pieces of `k`
+// consecutive leaves in slab j. A reader thread preads an item's pieces into one
+// of its own pinned buffers (k*S bytes) and at once queues one 2-D host-to-device
+// copy of them on its own stream, so copies of a few MiB follow the reads within
+// microseconds and the data crosses host memory while it is still cache-warm; a
+// thread reuses a buffer only after the copy that last read it is done, so no
+// reader runs more than `bufs` items ahead of its copies. Slab j is complete once
+// every reader has queued its items of it: s_copy then waits for all readers'
+// streams, and on_slab(j) queues the slab's hash pass.
+template <class OnSlab>
+tcx_status stage_pieces_from_files(tcx_group* g, const tcx_file_stage& fs, uint8_t* stage, uint64_t mine, uint64_t L,
+                                   uint64_t S, uint64_t J, uint64_t n_full, uint64_t tail, uint64_t k, int bufs,
+                                   OnSlab&& on_slab, Clock::time_point deadline) {
+  auto ctx = std::make_shared<FileStageCtx>();
+  if (tcx_status st = open_stage_files(fs, mine, ctx.get()); st != TCX_OK) return st;
+  const int nt = reader_count(fs);
+  ensure_readers(g, nt);
+  if (tcx_status st = ensure_piece_buffers(g, nt, k * S, bufs); st != TCX_OK) return st;
+  // The copies into the staged buffer wait for the caller's earlier work on it.
+  for (cudaStream_t s : g->rd_streams) TCX_CUDA_TRY(cudaStreamWaitEvent(s, g->ev_start, 0));
+
+  const uint64_t n_rows = n_full + (tail > 0 ? 1 : 0);
+  const uint64_t n_items = (n_rows + k - 1) / k;
+  const int device = g->device;
+  std::vector<std::shared_ptr<ReadBatch>> batches(J);
+  for (uint64_t j = 0; j < J; ++j) {
+    auto b = std::make_shared<ReadBatch>();
+    b->n = n_items;
+    b->fn = [g, ctx, stage, j, S, L, n_full, n_rows, tail, k, bufs, device, deadline](uint64_t i,
+                                                                                       ReadBatch& bb) -> bool {
+      const uint64_t off = j * S, r0 = i * k, r1 = std::min(r0 + k, n_rows);
+      const uint64_t full1 = std::min(r1, n_full);  // full leaves of the item: [r0, full1)
+      const bool full_part = r0 < full1 && off < L;
+      const bool tail_part = r1 > n_full && tail > off;  // the short last leaf is in the item
+      if (!full_part && !tail_part) return true;
+      const int t = t_reader;
+      if (t < 0 || t >= static_cast<int>(g->rd_streams.size())) {
+        bb.fail(TCX_INTERNAL, "staged piece read outside the group's reader threads");
+        return false;
+      }
+      if (cudaError_t e = cudaSetDevice(device); e != cudaSuccess) {
+        cudaGetLastError();
+        bb.fail(TCX_INTERNAL, "reader thread cudaSetDevice: " + cuda_msg(e));
+        return false;
+      }
+      const uint64_t slot = static_cast<uint64_t>(t) * bufs + g->rd_count[t]++ % bufs;
+      if (g->rd_used[slot] && !wait_piece_copy(g->rd_events[slot], deadline, bb)) return false;
+      uint8_t* buf = g->h_pieces + slot * g->piece_bytes;
+      const uint64_t w = full_part ? std::min(S, L - off) : 0;
+      const uint64_t wt = tail_part ? std::min(S, tail - off) : 0;
+      for (uint64_t r = r0; r < full1 && full_part; ++r)
+        if (!read_stage_range(*ctx, r * L + off, w, buf + (r - r0) * S, bb)) return false;
+      if (tail_part && !read_stage_range(*ctx, n_full * L + off, wt, buf + (n_full - r0) * S, bb)) return false;
+      cudaStream_t s = g->rd_streams[t];
+      cudaError_t e = cudaSuccess;
+      if (full_part)
+        e = full1 - r0 == 1 ? cudaMemcpyAsync(stage + r0 * L + off, buf, w, cudaMemcpyHostToDevice, s)
+                            : cudaMemcpy2DAsync(stage + r0 * L + off, L, buf, S, w, full1 - r0, cudaMemcpyHostToDevice, s);
+      if (e == cudaSuccess && tail_part)
+        e = cudaMemcpyAsync(stage + n_full * L + off, buf + (n_full - r0) * S, wt, cudaMemcpyHostToDevice, s);
+      if (e == cudaSuccess) e = cudaEventRecord(g->rd_events[slot], s);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        bb.fail(TCX_INTERNAL, "queueing the host-to-device copy of staged pieces: " + cuda_msg(e));
+        return false;
+      }
+      g->rd_used[slot] = 1;
+      return true;
+    };
+    batches[j] = b;
+    g->readers->submit(b);
+  }
+  tcx_status st = TCX_OK;
+  for (uint64_t j = 0; j < J && st == TCX_OK; ++j) {
+    if (!ReadPool::wait(*batches[j], deadline)) {
+      st = set_error(TCX_DEADLINE_EXCEEDED, "reading the staged range from files timed out");
+      break;
+    }
+    if (batches[j]->failed) {
+      std::lock_guard<std::mutex> lk(batches[j]->mu);
+      st = set_error(batches[j]->code != TCX_OK ? batches[j]->code : TCX_INTERNAL, batches[j]->err);
+      break;
+    }
+    for (int t = 0; t < nt && st == TCX_OK; ++t) {
+      if (cudaEventRecord(g->rd_marks[t], g->rd_streams[t]) != cudaSuccess ||
+          cudaStreamWaitEvent(g->s_copy, g->rd_marks[t], 0) != cudaSuccess) {
+        cudaGetLastError();
+        st = set_error(TCX_INTERNAL, "joining the staged pieces' copies");
+      }
+    }
+    if (st == TCX_OK) st = on_slab(j);
+  }
+  if (st != TCX_OK) {
+    // Nothing of this load may still write into the piece buffers or the staged
+    // buffer once the call returns: skip what is not started, wait for reads in
+    // progress and for every queued copy.
+    for (auto& b : batches) b->failed = true;
+    for (auto& b : batches) ReadPool::wait(*b, Clock::now() + std::chrono::milliseconds(g->timeout_ms));
+    for (cudaStream_t s : g->rd_streams) cudaStreamSynchronize(s);
     cudaStreamSynchronize(g->s_copy);
     cudaGetLastError();
   }
@@ -1146,7 +1381,11 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
       const uint64_t n_full = mine / L, tail = mine - n_full * L;
       const uint64_t span = n_full > 0 ? L : tail;  // bytes per leaf to cover
       const uint64_t n_rows = n_full + (tail > 0 ? 1 : 0);
+      // From files, leaves of at least 2 pieces are staged piece by piece (each
+      // piece's copy queued as soon as it is read, see stage_pieces_from_files).
+      const uint64_t piece = files != nullptr ? piece_bytes_for(span) : 0;
       uint64_t S = plan->slab_bytes;
+      if (piece > 0 && S == 0) S = piece;
       if (S == 0 && files != nullptr) {
         // From files, a slab is one pinned slot: about slot_bytes per slab.
         // S is a power of two from 64 bytes up to the leaf.
@@ -1160,6 +1399,13 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
       if ((st = ensure_events(g->slab_events, J)) != TCX_OK) return st;
       // H2D of slab j from src (rows at src_pitch; the short leaf's piece at tsrc),
       // then the streamed hash pass over it.
+      // The streamed hash pass over slab j, once everything queued on s_copy is done.
+      auto hash_slab = [&](uint64_t j) -> tcx_status {
+        TCX_CUDA_TRY(cudaEventRecord(g->slab_events[j], g->s_copy));
+        TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_hash, g->slab_events[j], 0));
+        return launch_leaf_pass(stage, mine, L, static_cast<uint32_t>(n_mine), j * S, S,
+                                static_cast<uint32_t*>(g->states.p), g->digests_mine.p, g->s_hash);
+      };
       auto enqueue_slab = [&](uint64_t j, const uint8_t* src, uint64_t src_pitch, const uint8_t* tsrc) -> tcx_status {
         const uint64_t off = j * S;
         if (n_full > 0 && off < L) {
@@ -1170,10 +1416,7 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
           const uint64_t w = std::min(S, tail - off);
           TCX_CUDA_TRY(cudaMemcpyAsync(stage + n_full * L + off, tsrc, w, cudaMemcpyHostToDevice, g->s_copy));
         }
-        TCX_CUDA_TRY(cudaEventRecord(g->slab_events[j], g->s_copy));
-        TCX_CUDA_TRY(cudaStreamWaitEvent(g->s_hash, g->slab_events[j], 0));
-        return launch_leaf_pass(stage, mine, L, static_cast<uint32_t>(n_mine), off, S,
-                                static_cast<uint32_t*>(g->states.p), g->digests_mine.p, g->s_hash);
+        return hash_slab(j);
       };
       if (files == nullptr) {
         for (uint64_t j = 0; j < J; ++j) {
@@ -1181,7 +1424,11 @@ tcx_status group_load(tcx_group* g, const tcx_load_plan* plan, const void* h_sta
         }
       } else {
         const auto t_read = Clock::now();
-        st = stage_from_files(g, *files, mine, L, S, J, n_full, tail, enqueue_slab, deadline);
+        if (piece > 0 && S == piece)
+          st = stage_pieces_from_files(g, *files, stage, mine, L, S, J, n_full, tail, piece_rows_for(S, n_rows),
+                                       piece_buffers(), hash_slab, deadline);
+        else
+          st = stage_from_files(g, *files, mine, L, S, J, n_full, tail, enqueue_slab, deadline);
         read_ms = std::chrono::duration<float, std::milli>(Clock::now() - t_read).count();
         if (st != TCX_OK) return st;
       }

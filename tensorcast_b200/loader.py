@@ -203,8 +203,10 @@ class Group:
 
         files: this rank's staged range as (path, file_offset, stage_offset, length) segments
         (stage offsets relative to bounds[rank]; uncovered bytes are zero): the range is read
-        inside the call by the group's reader threads into a ring of pinned slots, overlapped
-        with the copies to the device and the hash (tcx_group_load_files).
+        inside the call by the group's reader threads, overlapped with the copies to the device
+        and the hash (tcx_group_load_files). Leaves of at least 128 KiB are read in pieces (up to 256 KiB
+        of a few consecutive leaves per 4 MiB copy, each reader with two pinned buffers); shorter
+        leaves in slabs through a ring of ring_slots pinned slots of about slot_bytes each.
 
         peer_push: exchange by copying into the peers' views over NVLink (d_view must be a
         cudaMalloc allocation, e.g. a torch CUDA tensor); push_nccl_share (0..1): that share of

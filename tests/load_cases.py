@@ -30,14 +30,15 @@ def run_cases(group, world: int, rank: int, gather, tmpdir: str, log=print) -> i
     bind-into targets case. gather(jobs) returns every rank's jobs. Returns the failures."""
     failures = 0
     llama = llama_tensors()
-    cases = [("llama", llama, 1 << 16)]
+    # 64 KiB leaves stage from files in slabs, 256 KiB leaves in pieces.
+    cases = [("llama", llama, 1 << 16), ("llama_pieces", llama, 1 << 18)]
     for seed in range(3):
         cases.append((f"random{seed}", random_tensors(100 + seed, n=24),
                       int(np.random.default_rng(seed).choice([64, 512, 4096]))))
     for name, tensors, leaf in cases:
         canon, meta = oviews.canonical_bytes(tensors)
         index = index_from_meta(meta, canon.size)
-        if name == "llama":
+        if name.startswith("llama"):
             sl = oviews.tp_slices(meta, world, rank)
             o = "model.layers.1.self_attn.o_proj.weight"
             sl.pop(o)

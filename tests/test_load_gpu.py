@@ -296,7 +296,8 @@ def test_file_staged_load_matches_oracle(cuda_device, tmp_path, threads, slot_by
         g.close()
 
 
-def test_file_staged_load_errors_then_recovers(cuda_device, tmp_path):
+def test_file_staged_load_errors_then_recovers(cuda_device, tmp_path, monkeypatch):
+    monkeypatch.setenv("TCX_STAGE", "slabs")  # the slab ring (leaves this long default to pieces)
     canon = np.random.default_rng(5).integers(0, 256, size=(3 << 20) + 4000, dtype=np.uint8)
     path = tmp_path / "a.bin"
     path.write_bytes(canon.tobytes())
@@ -320,5 +321,93 @@ def test_file_staged_load_errors_then_recovers(cuda_device, tmp_path):
                      files=[(str(path), 0, 0, canon.size)], **kw)
         assert res["root"] == oracle.tree_root(oracle.leaf_digests(canon, leaf))
         assert res["stage_read_ms"] > 0
+    finally:
+        g.close()
+
+
+def _random_segments(tmp_path, canon, rng, n_files=2):
+    """Covers canon with file segments of random lengths in two files (junk before each
+    segment); holes between segments are zeroed in canon, as the loader fills them."""
+    bufs = [bytearray(int(rng.integers(0, 64))) for _ in range(n_files)]
+    segs, pos, k = [], 0, 0
+    while pos < canon.size:
+        hole = int(rng.integers(0, 100)) if rng.random() < 0.3 else 0
+        canon[pos:pos + hole] = 0
+        pos = min(canon.size, pos + hole)
+        ln = min(int(rng.integers(1000, 300000)), canon.size - pos)
+        if ln <= 0:
+            break
+        f = k % n_files
+        bufs[f] += bytes(int(rng.integers(0, 24)))
+        segs.append((str(tmp_path / f"piece{f}.bin"), len(bufs[f]), pos, ln))
+        bufs[f] += canon[pos:pos + ln].tobytes()
+        pos += ln
+        k += 1
+    for f in range(n_files):
+        (tmp_path / f"piece{f}.bin").write_bytes(bytes(bufs[f]))
+    return segs
+
+
+@pytest.mark.parametrize("threads,bufs,leaf,copy", [(1, 1, 1 << 18, 1 << 16), (4, 3, 1 << 17, 3 << 16),
+                                                     (7, 2, (1 << 18) + 4096, 1 << 20), (3, 2, 1 << 18, 1 << 30)])
+def test_piece_staged_load_matches_oracle(cuda_device, tmp_path, monkeypatch, threads, bufs, leaf, copy):
+    """Piece staging (each reader queues one host-to-device copy of the pieces of a few
+    consecutive leaves it has read, on its own stream, from a few reused pinned buffers):
+    several files with holes and junk, a short last leaf alone or inside a group, one leaf
+    per copy up to all leaves in one copy, one to seven readers; root, staged bytes and a
+    strided view bit-exact, and the same group loads again after the reader count changes."""
+    from viewtools import apply_jobs
+    monkeypatch.setenv("TCX_STAGE", "pieces")
+    monkeypatch.setenv("TCX_STAGE_PIECE", str(1 << 16))
+    monkeypatch.setenv("TCX_STAGE_PIECE_BUFS", str(bufs))
+    monkeypatch.setenv("TCX_STAGE_COPY", str(copy))
+    rng = np.random.default_rng(threads)
+    canon = rng.integers(0, 256, size=5 * leaf + 12345, dtype=np.uint8)
+    segs = _random_segments(tmp_path, canon, rng)
+    jobs = np.zeros(3, JOB_DTYPE)
+    jobs[0] = (1000, 0, 2048, 1024, 1024, 300)          # a strided 2-D piece
+    jobs[1] = (canon.size - 5000, 300 * 1024, 0, 0, 5000, 1)  # the short last leaf's end
+    jobs[2] = (3 * leaf - 7, 300 * 1024 + 5000, 0, 0, 777, 1)  # across a leaf boundary
+    view_bytes = 300 * 1024 + 5000 + 777
+    want = np.zeros(view_bytes, np.uint8)
+    apply_jobs(canon, want, jobs)
+    g = Group(1, 0, 0)
+    try:
+        for nt in (threads, threads + 2):
+            d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+            d_view = torch.zeros(view_bytes, dtype=torch.uint8, device="cuda")
+            res = g.load(canon.size, leaf, [0, canon.size], [jobs], d_stage=d_stage, d_view=d_view, files=segs,
+                         view_bytes=view_bytes, read_threads=nt)
+            assert res["root"] == oracle.tree_root(oracle.leaf_digests(canon, leaf))
+            assert (d_stage.cpu().numpy() == canon).all()
+            assert (d_view.cpu().numpy() == want).all()
+            assert res["stage_read_ms"] > 0
+    finally:
+        g.close()
+
+
+def test_piece_staged_load_errors_then_recovers(cuda_device, tmp_path, monkeypatch):
+    monkeypatch.setenv("TCX_STAGE", "pieces")
+    monkeypatch.setenv("TCX_STAGE_PIECE", str(1 << 16))
+    canon = np.random.default_rng(6).integers(0, 256, size=(3 << 20) + 4000, dtype=np.uint8)
+    path = tmp_path / "a.bin"
+    path.write_bytes(canon.tobytes())
+    leaf = 1 << 18
+    g = Group(1, 0, 0)
+    try:
+        d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+        d_view = torch.zeros(canon.size, dtype=torch.uint8, device="cuda")
+        whole = np.zeros(1, JOB_DTYPE)
+        whole[0] = (0, 0, 0, 0, canon.size, 1)
+        kw = dict(d_stage=d_stage, d_view=d_view, view_bytes=canon.size, read_threads=3)
+        short = tmp_path / "short.bin"
+        short.write_bytes(canon[: canon.size - 100].tobytes())
+        with pytest.raises(_native.TcxError) as e:
+            g.load(canon.size, leaf, [0, canon.size], [whole], files=[(str(short), 0, 0, canon.size)], **kw)
+        assert e.value.code == _native.DATA_LOSS and "short read" in e.value.message
+        res = g.load(canon.size, leaf, [0, canon.size], [whole], files=[(str(path), 0, 0, canon.size)], **kw)
+        assert res["root"] == oracle.tree_root(oracle.leaf_digests(canon, leaf))
+        assert (d_stage.cpu().numpy() == canon).all()
+        assert (d_view.cpu().numpy() == canon).all()
     finally:
         g.close()
