@@ -14,12 +14,24 @@
 //
 // A group is a whole number of leaves, so every leaf is hashed in one launch
 // and groups are independent; `depth` slots (pinned + device buffer + stream)
-// keep reads, copies and hashing of different groups in flight at once. The
-// slots stay allocated per device between calls (tcx_file_hash_release frees
-// them); calls on one device are serialised.
+// keep reads, copies and hashing of different groups in flight at once.
+//
+// Leaves of two pieces or more are streamed instead (hash_file_segments_streamed):
+// the leaves go in waves of up to 4096, and slab j of a wave is the 256 KiB piece
+// j of each of its leaves. Reader threads pread the pieces of a few consecutive
+// leaves into one of their own pinned buffers and queue its copy into a device
+// slab buffer at once (as the collective load does); once a slab is on the
+// device one pass of the leaf kernel advances every chain of the wave over it,
+// so thousands of chains hash at once from a ring of three slab buffers instead
+// of a few hundred per 1 GiB group.
+//
+// The buffers stay allocated per device between calls (tcx_file_hash_release
+// frees them); calls on one device are serialised.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -27,6 +39,7 @@
 #include <thread>
 #include <vector>
 
+#include "staging.h"
 #include "tcx_internal.h"
 
 namespace tcx {
@@ -34,6 +47,15 @@ namespace {
 
 constexpr uint64_t kDefaultGroupBytes = 1ull << 30;
 constexpr int kDefaultDepth = 4;
+
+// Streamed hashing: bytes of one leaf per slab, bytes per host-to-device copy,
+// pinned buffers per reader thread, device slab buffers and their total bytes.
+constexpr uint64_t kPieceBytes = 256ull << 10;
+constexpr uint64_t kMinPieceBytes = 64ull << 10;
+constexpr uint64_t kPieceCopy = 4ull << 20;
+constexpr int kPieceBufs = 2;
+constexpr int kSlabRing = 3;
+constexpr uint64_t kSlabRingBytes = 3ull << 30;  // TCX_HASH_WAVE_LEAVES overrides the leaves per wave
 
 struct Slot {
   uint8_t* host = nullptr;
@@ -54,6 +76,67 @@ struct FileHashContext {
   uint8_t* scratch = nullptr;
   uint64_t scratch_bytes = 0;
   uint8_t* root = nullptr;
+  // Streamed hashing.
+  std::unique_ptr<ReadPool> readers;
+  PieceBuffers pieces;
+  uint8_t* ring = nullptr;  // kSlabRing slab buffers
+  uint64_t ring_bytes = 0;
+  std::vector<cudaEvent_t> ring_free;  // per slab buffer: the pass that last read it
+  std::vector<cudaEvent_t> wave_done;  // per wave: its leaf digests written
+  cudaStream_t s_hash = nullptr;
+  uint32_t* states = nullptr;
+  uint64_t states_bytes = 0;
+
+  void free_stream() {
+    readers.reset();  // joins the reader threads before their buffers go away
+    pieces.release();
+    if (s_hash) cudaStreamSynchronize(s_hash);
+    for (auto* v : {&ring_free, &wave_done}) {
+      for (cudaEvent_t e : *v) cudaEventDestroy(e);
+      v->clear();
+    }
+    if (s_hash) cudaStreamDestroy(s_hash);
+    s_hash = nullptr;
+    if (ring) cudaFree(ring);
+    ring = nullptr;
+    ring_bytes = 0;
+    if (states) cudaFree(states);
+    states = nullptr;
+    states_bytes = 0;
+  }
+  tcx_status ensure_stream(int n_readers, uint64_t piece_buf, uint64_t ring_total, uint64_t n_states_bytes,
+                           uint64_t n_waves) {
+    if (!readers || readers->size() != n_readers) {
+      readers.reset();
+      readers = std::make_unique<ReadPool>(n_readers);
+    }
+    if (tcx_status st = pieces.ensure(n_readers, piece_buf, kPieceBufs); st != TCX_OK) return st;
+    if (s_hash == nullptr) TCX_CUDA_TRY(cudaStreamCreateWithFlags(&s_hash, cudaStreamNonBlocking));
+    while (ring_free.size() < static_cast<size_t>(kSlabRing) || wave_done.size() < n_waves) {
+      cudaEvent_t e;
+      TCX_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      (ring_free.size() < static_cast<size_t>(kSlabRing) ? ring_free : wave_done).push_back(e);
+    }
+    if (ring_bytes < ring_total) {
+      if (ring) cudaFree(ring);
+      ring = nullptr;
+      ring_bytes = 0;
+      if (cudaError_t e = cudaMalloc(&ring, ring_total); e != cudaSuccess) {
+        cudaGetLastError();
+        return set_errorf(TCX_RESOURCE_EXHAUSTED, "file hash slab buffers of %llu bytes: %s",
+                          static_cast<unsigned long long>(ring_total), cuda_msg(e).c_str());
+      }
+      ring_bytes = ring_total;
+    }
+    if (states_bytes < n_states_bytes) {
+      if (states) cudaFree(states);
+      states = nullptr;
+      states_bytes = 0;
+      TCX_CUDA_TRY(cudaMalloc(&states, n_states_bytes));
+      states_bytes = n_states_bytes;
+    }
+    return TCX_OK;
+  }
 
   void free_slots() {
     for (auto& s : slots) {
@@ -67,12 +150,31 @@ struct FileHashContext {
     slot_bytes = 0;
   }
   void free_all() {
+    free_stream();
     free_slots();
     if (digests) cudaFree(digests);
     if (scratch) cudaFree(scratch);
     if (root) cudaFree(root);
     digests = scratch = root = nullptr;
     digest_bytes = scratch_bytes = 0;
+  }
+  tcx_status ensure_common(uint64_t n_digest_bytes, uint64_t n_scratch_bytes) {
+    if (digest_bytes < n_digest_bytes) {
+      if (digests) cudaFree(digests);
+      digests = nullptr;
+      digest_bytes = 0;
+      TCX_CUDA_TRY(cudaMalloc(&digests, n_digest_bytes));
+      digest_bytes = n_digest_bytes;
+    }
+    if (scratch_bytes < n_scratch_bytes) {
+      if (scratch) cudaFree(scratch);
+      scratch = nullptr;
+      scratch_bytes = 0;
+      TCX_CUDA_TRY(cudaMalloc(&scratch, n_scratch_bytes));
+      scratch_bytes = n_scratch_bytes;
+    }
+    if (root == nullptr) TCX_CUDA_TRY(cudaMalloc(&root, 256));
+    return TCX_OK;
   }
   tcx_status ensure(int n_slots, uint64_t bytes, uint64_t n_digest_bytes, uint64_t n_scratch_bytes) {
     if (static_cast<int>(slots.size()) < n_slots || slot_bytes < bytes) {
@@ -93,27 +195,14 @@ struct FileHashContext {
       }
     }
     for (auto& s : slots) s.group = -1;
-    if (digest_bytes < n_digest_bytes) {
-      if (digests) cudaFree(digests);
-      digests = nullptr;
-      digest_bytes = 0;
-      TCX_CUDA_TRY(cudaMalloc(&digests, n_digest_bytes));
-      digest_bytes = n_digest_bytes;
-    }
-    if (scratch_bytes < n_scratch_bytes) {
-      if (scratch) cudaFree(scratch);
-      scratch = nullptr;
-      scratch_bytes = 0;
-      TCX_CUDA_TRY(cudaMalloc(&scratch, n_scratch_bytes));
-      scratch_bytes = n_scratch_bytes;
-    }
-    if (root == nullptr) TCX_CUDA_TRY(cudaMalloc(&root, 256));
-    return TCX_OK;
+    return ensure_common(n_digest_bytes, n_scratch_bytes);
   }
   // After an error: nothing of this call may still run when the buffers are next used.
   void drain() {
     for (auto& s : slots)
       if (s.stream) cudaStreamSynchronize(s.stream);
+    pieces.sync();
+    if (s_hash) cudaStreamSynchronize(s_hash);
   }
 };
 
@@ -208,6 +297,147 @@ tcx_status hash_file_segments(FileHashContext& r, const tcx_file_segment* segs, 
   return report_done(n_groups, true);
 }
 
+// Piece size for leaves of `leaf` bytes in a stream of `total`, 0 for the group
+// path: a power of two from 64 KiB up to 256 KiB and at most half a leaf.
+uint64_t stream_piece_bytes(uint64_t leaf, uint64_t total, uint64_t read_flags) {
+  if (read_flags & TCX_READ_DIRECT) return 0;  // O_DIRECT windows go through the group path
+  if (const char* m = std::getenv("TCX_STAGE"); m != nullptr && std::strcmp(m, "slabs") == 0) return 0;
+  const uint64_t span = std::min(leaf, total);
+  uint64_t S = kMinPieceBytes;
+  while (S * 2 <= kPieceBytes && S * 4 <= span) S *= 2;
+  return S * 2 <= span ? S : 0;
+}
+
+tcx_status hash_file_segments_streamed(FileHashContext& r, const tcx_file_segment* segs, uint64_t n_segs,
+                                       uint64_t total, uint64_t L, uint64_t S, int read_threads, int device,
+                                       tcx_progress_fn progress, void* progress_ctx, uint8_t root[32]) {
+  const uint64_t n_full = total / L, tail = total - n_full * L;
+  const uint64_t n_leaves = n_full + (tail > 0 ? 1 : 0);
+  const uint64_t J = (std::min(L, total) + S - 1) / S;  // slabs per wave
+  uint64_t W = std::max<uint64_t>(1, kSlabRingBytes / (kSlabRing * S));  // leaves per wave
+  if (const char* v = std::getenv("TCX_HASH_WAVE_LEAVES")) W = std::max<uint64_t>(1, std::strtoull(v, nullptr, 0));
+  W = std::min<uint64_t>(W, n_leaves);
+  const uint64_t n_waves = (n_leaves + W - 1) / W;
+  const uint64_t k = std::max<uint64_t>(1, std::min<uint64_t>(W, kPieceCopy / S));  // leaves per copy
+  const uint64_t slab_bytes = W * S;
+  const int nt = read_threads > 0 ? read_threads : std::max(1, std::min(16, affinity_cpus()));
+  if (tcx_status st = r.ensure_common(n_leaves * 32, std::max<uint64_t>(merkle_scratch_bytes(n_leaves), 256));
+      st != TCX_OK)
+    return st;
+  if (tcx_status st = r.ensure_stream(nt, k * S, kSlabRing * slab_bytes, W * 32, n_waves); st != TCX_OK) return st;
+  auto ctx = std::make_shared<FileStageCtx>();
+  if (tcx_status st = open_stage_files(segs, n_segs, total, ctx.get()); st != TCX_OK) return st;
+  // The call has no deadline of its own (the CPU path it replaces blocks until
+  // its reads return); this bounds only the wait for a stuck copy.
+  const auto deadline = StageClock::now() + std::chrono::hours(24);
+
+  PieceBuffers& pb = r.pieces;
+  const uint64_t Q = n_waves * J;  // slabs in stream order: wave-major
+  std::vector<std::shared_ptr<ReadBatch>> batches(Q);
+  auto submit = [&](uint64_t q) {
+    const uint64_t w = q / J, j = q % J, w0 = w * W, ww = std::min(W, n_leaves - w0);
+    uint8_t* slab = r.ring + (q % kSlabRing) * slab_bytes;
+    cudaEvent_t free_ev = r.ring_free[q % kSlabRing];
+    auto b = std::make_shared<ReadBatch>();
+    b->n = (ww + k - 1) / k;
+    b->fn = [&pb, ctx, slab, free_ev, w0, ww, j, S, L, n_full, tail, k, device, deadline](uint64_t i,
+                                                                                         ReadBatch& bb) -> bool {
+      const uint64_t off = j * S, r0 = i * k, r1 = std::min(ww, r0 + k);
+      uint64_t used = 0;  // rows of the item up to the last one with bytes in this slab
+      for (uint64_t r = r0; r < r1; ++r)
+        if ((w0 + r < n_full ? L : tail) > off) used = r - r0 + 1;
+      if (used == 0) return true;
+      const int t = reader_for_copies(pb, device, bb);
+      if (t < 0) return false;
+      uint64_t slot = 0;
+      uint8_t* buf = pb.acquire(t, deadline, bb, &slot);
+      if (buf == nullptr) return false;
+      for (uint64_t r = r0; r < r0 + used; ++r) {
+        const uint64_t len = w0 + r < n_full ? L : tail;
+        if (len > off && !read_stage_range(*ctx, (w0 + r) * L + off, std::min(S, len - off), buf + (r - r0) * S, bb))
+          return false;
+      }
+      // Rows at pitch S on both sides: one copy; the bytes past a short leaf's end
+      // are never read by the pass.
+      cudaStream_t st = pb.streams[t];
+      cudaError_t e = cudaStreamWaitEvent(st, free_ev, 0);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(slab + r0 * S, buf, used * S, cudaMemcpyHostToDevice, st);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        bb.fail(TCX_INTERNAL, "queueing the host-to-device copy of hashed pieces: " + cuda_msg(e));
+        return false;
+      }
+      return pb.queued(t, slot, bb);
+    };
+    batches[q] = b;
+    r.readers->submit(b);
+  };
+
+  if (progress) progress(0, total, progress_ctx);
+  uint64_t reported = 0;  // waves whose digests are known to be written
+  auto report_done = [&](uint64_t limit, bool wait) -> tcx_status {
+    while (reported < limit) {
+      const cudaError_t q = wait ? cudaEventSynchronize(r.wave_done[reported]) : cudaEventQuery(r.wave_done[reported]);
+      if (q == cudaErrorNotReady) break;
+      if (q != cudaSuccess) return set_error(TCX_INTERNAL, std::string("leaf hashing failed: ") + cudaGetErrorString(q));
+      ++reported;
+      if (progress) progress(std::min(total, reported * W * L), total, progress_ctx);
+    }
+    return TCX_OK;
+  };
+
+  tcx_status st = TCX_OK;
+  uint64_t submitted = 0;
+  for (; submitted < std::min<uint64_t>(Q, kSlabRing); ++submitted) submit(submitted);
+  for (uint64_t q = 0; q < Q && st == TCX_OK; ++q) {
+    const uint64_t w = q / J, j = q % J, w0 = w * W, ww = std::min(W, n_leaves - w0);
+    if (!ReadPool::wait(*batches[q], deadline)) {
+      st = set_error(TCX_DEADLINE_EXCEEDED, "reading the hashed files timed out");
+      break;
+    }
+    if (batches[q]->failed) {
+      std::lock_guard<std::mutex> lk(batches[q]->mu);
+      st = batches[q]->code == TCX_DATA_LOSS ? set_error(TCX_DATA_LOSS, "short read while hashing source")
+                                             : set_error(batches[q]->code != TCX_OK ? batches[q]->code : TCX_INTERNAL,
+                                                         batches[q]->err);
+      break;
+    }
+    if ((st = pb.join(r.s_hash)) != TCX_OK) break;
+    st = launch_leaf_pass_pitched(r.ring + (q % kSlabRing) * slab_bytes, S, total - w0 * L, L,
+                                  static_cast<uint32_t>(ww), j * S, S, r.states, r.digests + w0 * 32, r.s_hash);
+    if (st != TCX_OK) break;
+    if (cudaError_t e = cudaEventRecord(r.ring_free[q % kSlabRing], r.s_hash); e != cudaSuccess) {
+      cudaGetLastError();
+      st = set_error(TCX_INTERNAL, "recording a slab pass: " + cuda_msg(e));
+      break;
+    }
+    if (j == J - 1) {
+      if (cudaError_t e = cudaEventRecord(r.wave_done[w], r.s_hash); e != cudaSuccess) {
+        cudaGetLastError();
+        st = set_error(TCX_INTERNAL, "recording a wave: " + cuda_msg(e));
+        break;
+      }
+    }
+    // The slab buffer of q is free for slab q + kSlabRing once this pass has run;
+    // its readers' copies wait for the event just recorded.
+    if (submitted < Q) submit(submitted++);
+    if ((st = report_done(j == J - 1 ? w + 1 : w, false)) != TCX_OK) break;
+  }
+  if (st != TCX_OK) {
+    for (uint64_t q = 0; q < submitted; ++q) batches[q]->failed = true;
+    for (uint64_t q = 0; q < submitted; ++q)
+      ReadPool::wait(*batches[q], StageClock::now() + std::chrono::minutes(10));
+    pb.sync();
+    cudaStreamSynchronize(r.s_hash);
+    cudaGetLastError();
+    return st;
+  }
+  if ((st = launch_merkle(r.digests, n_leaves, r.scratch, r.root, r.s_hash)) != TCX_OK) return st;
+  TCX_CUDA_TRY(cudaMemcpyAsync(root, r.root, 32, cudaMemcpyDeviceToHost, r.s_hash));
+  TCX_CUDA_TRY(cudaStreamSynchronize(r.s_hash));
+  return report_done(n_waves, true);
+}
+
 }  // namespace
 }  // namespace tcx
 
@@ -248,8 +478,12 @@ extern "C" tcx_status tcx_multihash_from_file_segments(const tcx_file_segment* s
   FileHashContext* ctx = context_for(device);
   std::lock_guard<std::mutex> lock(ctx->mu);
   uint8_t root[32];
-  const tcx_status st = hash_file_segments(*ctx, segs, n_segs, total, leaf_bytes, group_bytes, depth, read_threads,
-                                           read_flags, progress, progress_ctx, root);
+  const uint64_t piece = stream_piece_bytes(leaf_bytes, total, read_flags);
+  const tcx_status st =
+      piece > 0 ? hash_file_segments_streamed(*ctx, segs, n_segs, total, leaf_bytes, piece, read_threads, device,
+                                              progress, progress_ctx, root)
+                : hash_file_segments(*ctx, segs, n_segs, total, leaf_bytes, group_bytes, depth, read_threads,
+                                     read_flags, progress, progress_ctx, root);
   if (st != TCX_OK) {
     ctx->drain();
     return st;

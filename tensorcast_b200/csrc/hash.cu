@@ -50,6 +50,7 @@ struct LeafGeom {
   uint64_t leaf;
   const uint64_t* off;  // table mode when non-null
   const uint32_t* len;
+  uint64_t pitch;       // > 0: the pass's bytes of leaf i are at src + i * pitch (a slab buffer)
 };
 
 // Per-chain quantities of one pass. A pass covers [seg_off, seg_off + seg_len) of
@@ -59,6 +60,7 @@ struct LeafPass {
   uint64_t start;     // byte offset of the leaf in the source
   uint64_t leaf_len;  // bytes of this leaf
   uint64_t begin;     // first byte of the pass inside the leaf
+  uint64_t data;      // offset of that byte in the source buffer
   uint64_t nfull;     // full 64-byte blocks of leaf data in this pass
   uint32_t nb;        // blocks compressed in this pass (data + padding)
   bool active;        // the pass touches this leaf
@@ -80,6 +82,7 @@ __device__ __forceinline__ LeafPass leaf_pass(uint32_t i, uint32_t n_leaves, con
   if (seg_off >= p.leaf_len) return p;
   p.active = true;
   p.begin = seg_off;
+  p.data = g.pitch ? static_cast<uint64_t>(i) * g.pitch : p.start + seg_off;
   const uint64_t room = p.leaf_len - seg_off;
   p.finalize = seg_len >= room;
   const uint64_t bytes = p.finalize ? room : seg_len;
@@ -122,7 +125,7 @@ __global__ void __launch_bounds__(kLeafThreads) sha256_leaf_kernel(const uint8_t
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const LeafPass ps = leaf_pass(i, n_leaves, geom, seg_off, seg_len);
   if (!ps.active) return;
-  const uint8_t* p = src + ps.start + ps.begin;
+  const uint8_t* p = src + ps.data;
   const uint64_t nfull = ps.nfull;
 
   uint32_t s[8];
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(64 * kWsPairs, 1) sha256_leaf_ws_kernel(const 
   const uint32_t bar_empty = bar_full + kWsStages;
 
   if (producer) {
-    const uint8_t* p = src + (ps.active ? ps.start + ps.begin : 0ull);
+    const uint8_t* p = src + (ps.active ? ps.data : 0ull);
     const uint4* q = reinterpret_cast<const uint4*>(p);
     uint4 cur[4], nxt[4];
     if (ps.active && ps.nfull > 0) {
@@ -606,15 +609,26 @@ static tcx_status launch_leaf_kernels(const uint8_t* src, const LeafGeom& geom, 
 
 tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, uint64_t seg_off,
                             uint64_t seg_len, uint32_t* states, void* d_digests, cudaStream_t stream) {
-  const LeafGeom geom{total, leaf, nullptr, nullptr};
+  const LeafGeom geom{total, leaf, nullptr, nullptr, 0};
   const bool vec = aligned16(d_src) && leaf % 16 == 0;
+  return launch_leaf_kernels(static_cast<const uint8_t*>(d_src), geom, n, vec, seg_off, seg_len, states,
+                             static_cast<uint8_t*>(d_digests), stream);
+}
+
+tcx_status launch_leaf_pass_pitched(const void* d_src, uint64_t pitch, uint64_t total, uint64_t leaf, uint32_t n,
+                                    uint64_t seg_off, uint64_t seg_len, uint32_t* states, void* d_digests,
+                                    cudaStream_t stream) {
+  if (pitch == 0 || pitch < std::min(seg_len, leaf))
+    return set_error(TCX_INVALID_ARGUMENT, "slab pitch is smaller than the pass");
+  const LeafGeom geom{total, leaf, nullptr, nullptr, pitch};
+  const bool vec = aligned16(d_src) && pitch % 16 == 0;
   return launch_leaf_kernels(static_cast<const uint8_t*>(d_src), geom, n, vec, seg_off, seg_len, states,
                              static_cast<uint8_t*>(d_digests), stream);
 }
 
 tcx_status launch_leaf_table(const void* d_src, const uint64_t* d_off, const uint32_t* d_len, uint32_t n,
                              bool offsets_aligned16, void* d_digests, cudaStream_t stream) {
-  const LeafGeom geom{0, 0, d_off, d_len};
+  const LeafGeom geom{0, 0, d_off, d_len, 0};
   const bool vec = aligned16(d_src) && offsets_aligned16;
   return launch_leaf_kernels(static_cast<const uint8_t*>(d_src), geom, n, vec, 0, ~0ull, nullptr,
                              static_cast<uint8_t*>(d_digests), stream);

@@ -42,6 +42,7 @@
 #include <thread>
 #include <vector>
 
+#include "staging.h"
 #include "tcx_internal.h"
 
 namespace tcx {
@@ -158,103 +159,6 @@ struct DevBuf {
   uint8_t* bytes() const { return static_cast<uint8_t*>(p); }
 };
 
-// One unit of host reading: fn(i) for i in [0, n), run by the reader pool's
-// threads; fn returns false (with code/err set under mu) on failure, after which
-// the remaining items are skipped.
-struct ReadBatch {
-  std::function<bool(uint64_t, ReadBatch&)> fn;
-  uint64_t n = 0;
-  std::atomic<uint64_t> done{0};
-  std::atomic<bool> failed{false};
-  uint64_t next = 0;  // next item to hand out (guarded by the pool's mutex)
-  std::mutex mu;
-  std::condition_variable cv;
-  tcx_status code = TCX_OK;
-  std::string err;
-  void fail(tcx_status c, const std::string& m) {
-    std::lock_guard<std::mutex> lk(mu);
-    if (code == TCX_OK) {
-      code = c;
-      err = m;
-    }
-    failed = true;
-  }
-};
-
-// Persistent host threads of a group that read file pieces into pinned slots.
-// Batches are served in submission order; a thread that finds every item of the
-// oldest batch handed out moves on to the next one, so several slabs are read
-// at once.
-// Index of the pool thread that runs the current item (-1 outside a pool).
-thread_local int t_reader = -1;
-
-class ReadPool {
- public:
-  explicit ReadPool(int n) {
-    for (int i = 0; i < n; ++i)
-      threads_.emplace_back([this, i] {
-        t_reader = i;
-        work();
-      });
-  }
-  ~ReadPool() {
-    {
-      std::lock_guard<std::mutex> lk(mu_);
-      stop_ = true;
-    }
-    cv_.notify_all();
-    for (auto& t : threads_) t.join();
-  }
-  int size() const { return static_cast<int>(threads_.size()); }
-  void submit(const std::shared_ptr<ReadBatch>& b) {
-    if (b->n == 0) return;
-    {
-      std::lock_guard<std::mutex> lk(mu_);
-      q_.push_back(b);
-    }
-    cv_.notify_all();
-  }
-  // True once every item of b has run (or been skipped after a failure); false at the deadline.
-  static bool wait(ReadBatch& b, std::chrono::steady_clock::time_point deadline) {
-    std::unique_lock<std::mutex> lk(b.mu);
-    return b.cv.wait_until(lk, deadline, [&] { return b.done.load() == b.n; });
-  }
-
- private:
-  void work() {
-    for (;;) {
-      std::shared_ptr<ReadBatch> b;
-      uint64_t i = 0;
-      {
-        std::unique_lock<std::mutex> lk(mu_);
-        cv_.wait(lk, [&] { return stop_ || !q_.empty(); });
-        if (q_.empty()) return;  // stop_ with nothing queued
-        b = q_.front();
-        i = b->next++;
-        if (b->next >= b->n) q_.pop_front();
-      }
-      if (!b->failed.load()) {
-        if (!b->fn(i, *b)) b->failed = true;
-      }
-      if (b->done.fetch_add(1) + 1 == b->n) {
-        std::lock_guard<std::mutex> lk(b->mu);
-        b->cv.notify_all();
-      }
-    }
-  }
-  std::mutex mu_;
-  std::condition_variable cv_;
-  std::deque<std::shared_ptr<ReadBatch>> q_;
-  std::vector<std::thread> threads_;
-  bool stop_ = false;
-};
-
-int affinity_cpus() {
-  cpu_set_t set;
-  CPU_ZERO(&set);
-  if (sched_getaffinity(0, sizeof set, &set) != 0) return 8;
-  return std::max(1, CPU_COUNT(&set));
-}
 
 }  // namespace
 
@@ -297,16 +201,9 @@ struct tcx_group {
   uint8_t* h_ring = nullptr;
   uint64_t h_ring_bytes = 0;
   std::unique_ptr<ReadPool> readers;
-  // Piece staging: each reader thread owns a stream and `piece_bufs` pinned
-  // buffers of `piece_bytes` (one leaf piece each), every buffer with the event of
-  // the copy that last read it; `rd_marks` join the readers' streams per slab.
-  uint8_t* h_pieces = nullptr;
-  uint64_t h_pieces_bytes = 0, piece_bytes = 0;
-  int piece_bufs = 0;
-  std::vector<cudaStream_t> rd_streams;
-  std::vector<cudaEvent_t> rd_events, rd_marks;
-  std::vector<uint8_t> rd_used;    // per buffer: a copy was queued from it
-  std::vector<uint64_t> rd_count;  // per reader: pieces read (picks the next buffer)
+  // Piece staging: per reader thread a stream and pinned buffers for the pieces
+  // of a few leaves, each with the event of the copy that last read it.
+  PieceBuffers pieces;
 };
 
 namespace {
@@ -673,15 +570,9 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   if (g->ev_push) cudaEventDestroy(g->ev_push);
   for (cudaStream_t s : g->s_peer)
     if (s) cudaStreamDestroy(s);
-  g->readers.reset();  // joins the reader threads before their ring goes away
-  for (cudaStream_t s : g->rd_streams)
-    if (s) cudaStreamSynchronize(s);
+  g->readers.reset();  // joins the reader threads before their buffers go away
+  g->pieces.release();
   if (g->h_ring) cudaFreeHost(g->h_ring);
-  if (g->h_pieces) cudaFreeHost(g->h_pieces);
-  for (auto* v : {&g->rd_events, &g->rd_marks})
-    for (cudaEvent_t e : *v) cudaEventDestroy(e);
-  for (cudaStream_t s : g->rd_streams)
-    if (s) cudaStreamDestroy(s);
   g->ipc_records.release();
   g->barrier_word.release();
   if (g->h_ipc) cudaFreeHost(g->h_ipc);
@@ -700,99 +591,6 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
 
 namespace {
 
-// One load's view of the files of the staged range, shared by the reader
-// threads (held by every batch of the load, so it outlives any piece in flight).
-struct FileStageCtx {
-  std::vector<tcx_file_segment> segs;  // sorted by dst_offset, non-overlapping; paths point into `paths`
-  std::vector<std::string> paths;
-  std::vector<int> fds;                 // per segment
-  std::vector<int> owned;               // distinct descriptors to close
-  ~FileStageCtx() {
-    for (int fd : owned) close(fd);
-  }
-};
-
-// Reads stage bytes [a, a + w) of the range into dst: file bytes where a segment
-// covers them, zero elsewhere (the canonical pads).
-bool read_stage_range(const FileStageCtx& c, uint64_t a, uint64_t w, uint8_t* dst, ReadBatch& b) {
-  const auto& sg = c.segs;
-  size_t k = std::partition_point(sg.begin(), sg.end(),
-                                  [&](const tcx_file_segment& x) { return x.dst_offset + x.length <= a; }) -
-             sg.begin();
-  uint64_t pos = a;
-  const uint64_t end = a + w;
-  while (pos < end) {
-    if (k >= sg.size() || sg[k].dst_offset >= end) {
-      std::memset(dst + (pos - a), 0, end - pos);
-      break;
-    }
-    const tcx_file_segment& x = sg[k];
-    if (x.dst_offset > pos) {
-      std::memset(dst + (pos - a), 0, x.dst_offset - pos);
-      pos = x.dst_offset;
-    }
-    const uint64_t e = std::min(end, x.dst_offset + x.length);
-    uint64_t got = 0;
-    const uint64_t want = e - pos, foff = x.file_offset + (pos - x.dst_offset);
-    while (got < want) {
-      const ssize_t r = pread(c.fds[k], dst + (pos - a) + got, want - got, static_cast<off_t>(foff + got));
-      if (r < 0 && errno == EINTR) continue;
-      if (r <= 0) {
-        char msg[512];
-        snprintf(msg, sizeof msg, "short read while staging %s at offset %llu (%llu of %llu bytes)", x.path,
-                 static_cast<unsigned long long>(foff + got), static_cast<unsigned long long>(got),
-                 static_cast<unsigned long long>(want));
-        b.fail(TCX_DATA_LOSS, msg);
-        return false;
-      }
-      got += static_cast<uint64_t>(r);
-    }
-    pos = e;
-    ++k;
-  }
-  return true;
-}
-
-// Streams this rank's staged range from files: reader threads pread slab j into
-// pinned slot j % K (row r of the slot = leaf r's piece of the slab), and as soon
-// as a slot is full its H2D and hash pass are queued; slot reuse waits for the
-// H2D of the slab that last used it. Reads of up to K slabs run ahead.
-// Checks, sorts and opens the segments of the staged range.
-tcx_status open_stage_files(const tcx_file_stage& fs, uint64_t mine, FileStageCtx* ctx) {
-  if (fs.n_segments > 0 && fs.segments == nullptr) return set_error(TCX_INVALID_ARGUMENT, "segments is null");
-  ctx->segs.reserve(fs.n_segments);
-  ctx->paths.reserve(fs.n_segments);
-  for (uint64_t i = 0; i < fs.n_segments; ++i) {
-    const tcx_file_segment& x = fs.segments[i];
-    if (x.path == nullptr) return set_errorf(TCX_INVALID_ARGUMENT, "segment %llu has no path", static_cast<unsigned long long>(i));
-    if (x.length == 0) continue;
-    if (x.dst_offset > mine || x.length > mine - x.dst_offset)
-      return set_errorf(TCX_INVALID_ARGUMENT, "segment %llu lies outside the staged range of %llu bytes",
-                        static_cast<unsigned long long>(i), static_cast<unsigned long long>(mine));
-    ctx->paths.emplace_back(x.path);
-    ctx->segs.push_back(x);
-  }
-  for (size_t i = 0; i < ctx->segs.size(); ++i) ctx->segs[i].path = ctx->paths[i].c_str();
-  std::sort(ctx->segs.begin(), ctx->segs.end(),
-            [](const tcx_file_segment& x, const tcx_file_segment& y) { return x.dst_offset < y.dst_offset; });
-  for (size_t i = 1; i < ctx->segs.size(); ++i)
-    if (ctx->segs[i].dst_offset < ctx->segs[i - 1].dst_offset + ctx->segs[i - 1].length)
-      return set_error(TCX_INVALID_ARGUMENT, "segments overlap in the staged range");
-  std::map<std::string, int> opened;
-  ctx->fds.resize(ctx->segs.size());
-  for (size_t i = 0; i < ctx->segs.size(); ++i) {
-    auto it = opened.find(ctx->segs[i].path);
-    if (it == opened.end()) {
-      const int fd = open(ctx->segs[i].path, O_RDONLY | O_CLOEXEC);
-      if (fd < 0) return set_errorf(TCX_NOT_FOUND, "open failed: %s", ctx->segs[i].path);
-      ctx->owned.push_back(fd);
-      it = opened.emplace(ctx->segs[i].path, fd).first;
-    }
-    ctx->fds[i] = it->second;
-  }
-  return TCX_OK;
-}
-
 // The group's reader pool with nt threads (kept between loads).
 void ensure_readers(tcx_group* g, int nt) {
   if (!g->readers || g->readers->size() != nt) {
@@ -807,7 +605,7 @@ template <class Enqueue>
 tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t mine, uint64_t L, uint64_t S, uint64_t J,
                             uint64_t n_full, uint64_t tail, Enqueue&& enqueue_slab, Clock::time_point deadline) {
   auto ctx = std::make_shared<FileStageCtx>();
-  if (tcx_status st = open_stage_files(fs, mine, ctx.get()); st != TCX_OK) return st;
+  if (tcx_status st = open_stage_files(fs.segments, fs.n_segments, mine, ctx.get()); st != TCX_OK) return st;
 
   const uint64_t n_rows = n_full + (tail > 0 ? 1 : 0);
   const uint64_t slot = n_rows * S;
@@ -870,60 +668,6 @@ tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t min
   return st;
 }
 
-// Per-reader streams, copy events and pinned piece buffers for piece staging.
-tcx_status ensure_piece_buffers(tcx_group* g, int nt, uint64_t S, int bufs) {
-  if (static_cast<int>(g->rd_streams.size()) == nt && g->piece_bufs == bufs && g->piece_bytes >= S) return TCX_OK;
-  for (cudaStream_t s : g->rd_streams) cudaStreamSynchronize(s);
-  for (auto* v : {&g->rd_events, &g->rd_marks}) {
-    for (cudaEvent_t e : *v) cudaEventDestroy(e);
-    v->clear();
-  }
-  for (cudaStream_t s : g->rd_streams) cudaStreamDestroy(s);
-  g->rd_streams.clear();
-  if (g->h_pieces) cudaFreeHost(g->h_pieces);
-  g->h_pieces = nullptr;
-  g->h_pieces_bytes = g->piece_bytes = 0;
-  g->piece_bufs = 0;
-  const uint64_t n = static_cast<uint64_t>(nt) * bufs;
-  if (cudaError_t e = cudaHostAlloc(&g->h_pieces, n * S, cudaHostAllocPortable); e != cudaSuccess) {
-    cudaGetLastError();
-    g->h_pieces = nullptr;
-    return set_errorf(TCX_RESOURCE_EXHAUSTED, "pinned piece buffers of %llu bytes: %s",
-                      static_cast<unsigned long long>(n * S), cuda_msg(e).c_str());
-  }
-  g->h_pieces_bytes = n * S;
-  for (int t = 0; t < nt; ++t) {
-    cudaStream_t s;
-    TCX_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
-    g->rd_streams.push_back(s);
-  }
-  if (tcx_status st = ensure_events(g->rd_events, n); st != TCX_OK) return st;
-  if (tcx_status st = ensure_events(g->rd_marks, nt); st != TCX_OK) return st;
-  g->rd_used.assign(n, 0);
-  g->rd_count.assign(nt, 0);
-  g->piece_bytes = S;
-  g->piece_bufs = bufs;
-  return TCX_OK;
-}
-
-// Waits, with a deadline, for the copy that last read a piece buffer.
-bool wait_piece_copy(cudaEvent_t e, Clock::time_point deadline, ReadBatch& b) {
-  for (;;) {
-    const cudaError_t q = cudaEventQuery(e);
-    if (q == cudaSuccess) return true;
-    if (q != cudaErrorNotReady) {
-      cudaGetLastError();
-      b.fail(TCX_INTERNAL, "host-to-device copy of a staged piece failed: " + cuda_msg(q));
-      return false;
-    }
-    if (Clock::now() > deadline) {
-      b.fail(TCX_DEADLINE_EXCEEDED, "host-to-device copy of a staged piece timed out");
-      return false;
-    }
-    std::this_thread::yield();
-  }
-}
-
 // Streams this rank's staged range from files in leaf pieces: piece (r, j) is
 // bytes [j*S, (j+1)*S) of leaf r, and a work item is the pieces of `k`
 // consecutive leaves in slab j. A reader thread preads an item's pieces into one
@@ -939,12 +683,13 @@ tcx_status stage_pieces_from_files(tcx_group* g, const tcx_file_stage& fs, uint8
                                    uint64_t S, uint64_t J, uint64_t n_full, uint64_t tail, uint64_t k, int bufs,
                                    OnSlab&& on_slab, Clock::time_point deadline) {
   auto ctx = std::make_shared<FileStageCtx>();
-  if (tcx_status st = open_stage_files(fs, mine, ctx.get()); st != TCX_OK) return st;
+  if (tcx_status st = open_stage_files(fs.segments, fs.n_segments, mine, ctx.get()); st != TCX_OK) return st;
   const int nt = reader_count(fs);
   ensure_readers(g, nt);
-  if (tcx_status st = ensure_piece_buffers(g, nt, k * S, bufs); st != TCX_OK) return st;
+  PieceBuffers& pb = g->pieces;
+  if (tcx_status st = pb.ensure(nt, k * S, bufs); st != TCX_OK) return st;
   // The copies into the staged buffer wait for the caller's earlier work on it.
-  for (cudaStream_t s : g->rd_streams) TCX_CUDA_TRY(cudaStreamWaitEvent(s, g->ev_start, 0));
+  if (tcx_status st = pb.wait_on(g->ev_start); st != TCX_OK) return st;
 
   const uint64_t n_rows = n_full + (tail > 0 ? 1 : 0);
   const uint64_t n_items = (n_rows + k - 1) / k;
@@ -953,46 +698,35 @@ tcx_status stage_pieces_from_files(tcx_group* g, const tcx_file_stage& fs, uint8
   for (uint64_t j = 0; j < J; ++j) {
     auto b = std::make_shared<ReadBatch>();
     b->n = n_items;
-    b->fn = [g, ctx, stage, j, S, L, n_full, n_rows, tail, k, bufs, device, deadline](uint64_t i,
-                                                                                       ReadBatch& bb) -> bool {
+    b->fn = [&pb, ctx, stage, j, S, L, n_full, n_rows, tail, k, device, deadline](uint64_t i, ReadBatch& bb) -> bool {
       const uint64_t off = j * S, r0 = i * k, r1 = std::min(r0 + k, n_rows);
       const uint64_t full1 = std::min(r1, n_full);  // full leaves of the item: [r0, full1)
       const bool full_part = r0 < full1 && off < L;
       const bool tail_part = r1 > n_full && tail > off;  // the short last leaf is in the item
       if (!full_part && !tail_part) return true;
-      const int t = t_reader;
-      if (t < 0 || t >= static_cast<int>(g->rd_streams.size())) {
-        bb.fail(TCX_INTERNAL, "staged piece read outside the group's reader threads");
-        return false;
-      }
-      if (cudaError_t e = cudaSetDevice(device); e != cudaSuccess) {
-        cudaGetLastError();
-        bb.fail(TCX_INTERNAL, "reader thread cudaSetDevice: " + cuda_msg(e));
-        return false;
-      }
-      const uint64_t slot = static_cast<uint64_t>(t) * bufs + g->rd_count[t]++ % bufs;
-      if (g->rd_used[slot] && !wait_piece_copy(g->rd_events[slot], deadline, bb)) return false;
-      uint8_t* buf = g->h_pieces + slot * g->piece_bytes;
+      const int t = reader_for_copies(pb, device, bb);
+      if (t < 0) return false;
+      uint64_t slot = 0;
+      uint8_t* buf = pb.acquire(t, deadline, bb, &slot);
+      if (buf == nullptr) return false;
       const uint64_t w = full_part ? std::min(S, L - off) : 0;
       const uint64_t wt = tail_part ? std::min(S, tail - off) : 0;
       for (uint64_t r = r0; r < full1 && full_part; ++r)
         if (!read_stage_range(*ctx, r * L + off, w, buf + (r - r0) * S, bb)) return false;
       if (tail_part && !read_stage_range(*ctx, n_full * L + off, wt, buf + (n_full - r0) * S, bb)) return false;
-      cudaStream_t s = g->rd_streams[t];
+      cudaStream_t s = pb.streams[t];
       cudaError_t e = cudaSuccess;
       if (full_part)
         e = full1 - r0 == 1 ? cudaMemcpyAsync(stage + r0 * L + off, buf, w, cudaMemcpyHostToDevice, s)
                             : cudaMemcpy2DAsync(stage + r0 * L + off, L, buf, S, w, full1 - r0, cudaMemcpyHostToDevice, s);
       if (e == cudaSuccess && tail_part)
         e = cudaMemcpyAsync(stage + n_full * L + off, buf + (n_full - r0) * S, wt, cudaMemcpyHostToDevice, s);
-      if (e == cudaSuccess) e = cudaEventRecord(g->rd_events[slot], s);
       if (e != cudaSuccess) {
         cudaGetLastError();
         bb.fail(TCX_INTERNAL, "queueing the host-to-device copy of staged pieces: " + cuda_msg(e));
         return false;
       }
-      g->rd_used[slot] = 1;
-      return true;
+      return pb.queued(t, slot, bb);
     };
     batches[j] = b;
     g->readers->submit(b);
@@ -1008,13 +742,7 @@ tcx_status stage_pieces_from_files(tcx_group* g, const tcx_file_stage& fs, uint8
       st = set_error(batches[j]->code != TCX_OK ? batches[j]->code : TCX_INTERNAL, batches[j]->err);
       break;
     }
-    for (int t = 0; t < nt && st == TCX_OK; ++t) {
-      if (cudaEventRecord(g->rd_marks[t], g->rd_streams[t]) != cudaSuccess ||
-          cudaStreamWaitEvent(g->s_copy, g->rd_marks[t], 0) != cudaSuccess) {
-        cudaGetLastError();
-        st = set_error(TCX_INTERNAL, "joining the staged pieces' copies");
-      }
-    }
+    st = pb.join(g->s_copy);
     if (st == TCX_OK) st = on_slab(j);
   }
   if (st != TCX_OK) {
@@ -1023,7 +751,7 @@ tcx_status stage_pieces_from_files(tcx_group* g, const tcx_file_stage& fs, uint8
     // progress and for every queued copy.
     for (auto& b : batches) b->failed = true;
     for (auto& b : batches) ReadPool::wait(*b, Clock::now() + std::chrono::milliseconds(g->timeout_ms));
-    for (cudaStream_t s : g->rd_streams) cudaStreamSynchronize(s);
+    pb.sync();
     cudaStreamSynchronize(g->s_copy);
     cudaGetLastError();
   }

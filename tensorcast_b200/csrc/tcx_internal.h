@@ -31,6 +31,12 @@ tcx_status launch_permute(const void* d_src, void* d_dst, const tcx_permute_job&
 tcx_status check_permute(const tcx_permute_job& pj);
 tcx_status launch_leaf_pass(const void* d_src, uint64_t total, uint64_t leaf, uint32_t n, uint64_t seg_off,
                             uint64_t seg_len, uint32_t* states, void* d_digests, cudaStream_t stream);
+// A pass over a slab buffer: bytes [seg_off, seg_off + seg_len) of leaf i (of
+// the leaves [0, n) of a stream of `total` bytes cut at `leaf`) are at
+// d_src + i * pitch.
+tcx_status launch_leaf_pass_pitched(const void* d_src, uint64_t pitch, uint64_t total, uint64_t leaf, uint32_t n,
+                                    uint64_t seg_off, uint64_t seg_len, uint32_t* states, void* d_digests,
+                                    cudaStream_t stream);
 tcx_status launch_merkle(const uint8_t* digests, uint64_t n, uint8_t* scratch, uint8_t* root, cudaStream_t stream);
 uint64_t merkle_scratch_bytes(uint64_t n);
 tcx_status preload_hash_kernels();

@@ -118,9 +118,12 @@ def test_disk_dir_hash_matches_reference_cases(cuda_device, tmp_path):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("stage", ["pieces", "slabs"])
 @pytest.mark.parametrize("group_bytes,depth", [(0, 0), (4 << 20, 2), (12 << 20, 3)])
-def test_disk_dir_hash_streams_many_groups(cuda_device, tmp_path, group_bytes, depth):
-    """Partitions with ragged sizes that straddle leaves and groups; several groups in flight."""
+def test_disk_dir_hash_streams_many_groups(cuda_device, tmp_path, monkeypatch, group_bytes, depth, stage):
+    """Partitions with ragged sizes that straddle leaves and groups; several groups in flight
+    (TCX_STAGE=slabs: whole-leaf groups; default: the leaves streamed in 256 KiB pieces)."""
+    monkeypatch.setenv("TCX_STAGE", stage)
     rng = np.random.default_rng(11)
     sizes = [5 << 20, 1, (3 << 20) + 17, 0, 9 << 20, 12345]
     blobs = [rng.integers(0, 256, n, dtype=np.uint8).tobytes() for n in sizes]
@@ -133,6 +136,41 @@ def test_disk_dir_hash_streams_many_groups(cuda_device, tmp_path, group_bytes, d
     assert got == oracle.multihash_from_cpu_memory(stream)
     assert seen[0] == (0, len(stream)) and seen[-1] == (len(stream), len(stream))
     assert all(a[0] <= b[0] for a, b in zip(seen, seen[1:]))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("leaf,wave,threads", [(1 << 18, 3, 2), (1 << 17, 1, 5), ((1 << 18) + 64, 7, 16)])
+def test_streamed_file_hash_in_waves(cuda_device, tmp_path, monkeypatch, leaf, wave, threads):
+    """The streamed path with waves of a few leaves (each slab a piece of every leaf of the wave,
+    copies of several leaves at once, a ring of three slab buffers reused many times), ragged
+    segments over three files and a short last leaf; equal to the CPU oracle with that leaf."""
+    monkeypatch.setenv("TCX_HASH_WAVE_LEAVES", str(wave))
+    rng = np.random.default_rng(leaf + wave)
+    data = rng.integers(0, 256, size=13 * leaf + 4321, dtype=np.uint8)
+    segs, pos, k = [], 0, 0
+    files = [bytearray() for _ in range(3)]
+    while pos < data.size:
+        ln = min(int(rng.integers(1, 400000)), data.size - pos)
+        f = k % 3
+        files[f] += bytes(int(rng.integers(0, 9)))
+        segs.append((str(tmp_path / f"s{f}.bin"), len(files[f]), pos, ln))
+        files[f] += data[pos:pos + ln].tobytes()
+        pos, k = pos + ln, k + 1
+    for f in range(3):
+        (tmp_path / f"s{f}.bin").write_bytes(bytes(files[f]))
+    seen = []
+    got = disk_hash.compute_data_multihash_from_segments(segs, data.size, leaf_chunk_bytes=leaf, read_threads=threads,
+                                                         progress_cb=lambda d, t: seen.append(d))
+    want = oracle.multihash(oracle.tree_root(oracle.leaf_digests(data, leaf)))
+    assert got == want
+    assert seen[0] == 0 and seen[-1] == data.size and seen == sorted(seen)
+    short = tmp_path / "short.bin"
+    short.write_bytes(data[: data.size - 10].tobytes())
+    with pytest.raises(disk_hash.DiskHashError, match="short read while hashing source"):
+        disk_hash.compute_data_multihash_from_segments([(str(short), 0, 0, data.size)], data.size,
+                                                       leaf_chunk_bytes=leaf, read_threads=threads)
+    assert disk_hash.compute_data_multihash_from_segments(segs, data.size, leaf_chunk_bytes=leaf,
+                                                          read_threads=threads) == want
 
 
 @pytest.mark.gpu
