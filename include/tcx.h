@@ -395,13 +395,17 @@ typedef void (*tcx_progress_fn)(uint64_t processed_bytes, uint64_t total_bytes, 
  * the stream [0, total) is given as file segments in stream order (dst_offset
  * = stream offset; they must tile [0, total) exactly), cut into leaves of
  * leaf_bytes (used as given, no adaptive policy, as the CPU path), SHA-256 per
- * leaf, Merkle tree, multihash. Groups of whole leaves (group_bytes, 0 = 1 GiB)
- * are read by read_threads parallel preads (0 = up to 16; read_flags as
- * tcx_read_segments_ex, e.g. TCX_READ_DIRECT) into `depth` pinned
- * slots (0 = 4), copied to the device and hashed on one stream per slot, so
- * reads, copies and hashing overlap. The slots stay allocated per device for
- * the next call (tcx_file_hash_release frees them); calls on one device are
- * serialised. Synchronous; restores the caller's current device. Errors as
+ * leaf, Merkle tree, multihash. Leaves of at least two 64 KiB pieces are
+ * streamed: in waves of up to 4096 leaves, read_threads reader threads (0 = up
+ * to 16) pread piece j (up to 256 KiB) of a few consecutive leaves into a pinned
+ * buffer and copy it at once into one of three device slab buffers; one pass
+ * of the leaf kernel per slab advances every chain of the wave. Otherwise (or
+ * with TCX_READ_DIRECT in read_flags, as tcx_read_segments_ex, or the
+ * environment variable TCX_STAGE=slabs), groups of whole leaves (group_bytes,
+ * 0 = 1 GiB) are read by parallel preads into `depth` pinned slots (0 = 4),
+ * copied and hashed on one stream per slot. Either way reads, copies and
+ * hashing overlap. The buffers stay allocated per device for the next call
+ * (tcx_file_hash_release frees them); calls on one device are serialised. Synchronous; restores the caller's current device. Errors as
  * the reference: total 0 or leaf 0 is
  * INVALID_ARGUMENT, a short read DATA_LOSS "short read while hashing source".
  * root_out (optional) receives the 32-byte root; out (>= 57 bytes) the

@@ -16,9 +16,11 @@ with the reference's rules (disk_artifact_context.cc:380-550):
   the payload bytes (disk_dir_hash.cc:91-95).
 
 The stream is cut into 4 MiB leaves as given (the CPU path applies no adaptive
-policy) and hashed by ``tcx_multihash_from_file_segments``: parallel preads into
-pinned slots, H2D and the SHA-256 leaf kernel per group of leaves, Merkle root on the
-device. The result equals the reference's CPU result bit for bit.
+policy) and hashed by ``tcx_multihash_from_file_segments``: the leaves in waves of up to
+4096, read in 256 KiB pieces by reader threads that copy each few leaves' pieces to the
+device at once, every chain of a wave advanced by one pass of the SHA-256 leaf kernel per
+slab, Merkle root on the device (short leaves, or ``direct_io``, in whole-leaf groups
+through pinned slots). The result equals the reference's CPU result bit for bit.
 """
 from __future__ import annotations
 
