@@ -687,6 +687,7 @@ def main() -> None:
                               "peak_gbs": h2d_peak,
                               "frac": round(T / file_ms / 1e6 / h2d_peak, 4) if h2d_peak else None,
                               "read_gbs": read_gbs,
+                              "topology": gpu_topology(world) if world > 1 else None,
                               "h2d_gbs_per_gpu_alone": h2d_solo if world > 1 else None,
                               "read_gbs_per_rank_alone": read_solo if world > 1 else None,
                               "h2d_gbs_per_gpu_all_at_once": round(h2d_peak / world, 2) if h2d_peak else None,
@@ -1015,6 +1016,33 @@ def exchange_summary(mode: str, recv: float, phase_ms: float, xfer_ms: float, nc
             "frac_of_measured_peer_copy_770": round(gbs / 770.0, 4), "exchange_and_view_ms": round(phase_ms, 3),
             "note": "received bytes per rank / the device time of the transfer (max over ranks); it runs beside the "
                     "leaf hash and the local extraction"}
+
+
+def gpu_topology(world: int):
+    """Where the N GPUs sit (queries only): PCI bus ids, the GPU-to-GPU link types and the CPU /
+    NUMA affinity columns of `nvidia-smi topo -m`, so that GPUs sharing a host bridge or a
+    socket can be told apart when the per-GPU H2D rates differ."""
+    out = {}
+    try:
+        r = subprocess.run(["nvidia-smi", "--query-gpu=index,pci.bus_id", "--format=csv,noheader"],
+                           capture_output=True, text=True, timeout=30)
+        ids = [ln.split(",")[1].strip() for ln in r.stdout.splitlines() if "," in ln]
+        out["pci_bus_ids"] = ids[:world]
+        r = subprocess.run(["nvidia-smi", "topo", "-m"], capture_output=True, text=True, timeout=30)
+        lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+        head = [h.strip() for h in lines[0].split("\t")] if lines else []
+        rows = {}
+        for ln in lines[1:]:
+            cols = [c.strip() for c in ln.split("\t")]
+            if cols and cols[0].startswith("GPU") and cols[0][3:].isdigit() and int(cols[0][3:]) < world:
+                named = dict(zip(head[1:], cols[1:]))
+                rows[cols[0]] = {"gpus": [named.get(f"GPU{j}", "?") for j in range(world)],
+                                 "cpu_affinity": named.get("CPU Affinity"), "numa": named.get("NUMA Affinity"),
+                                 "nics": {k: v for k, v in named.items() if k.startswith("NIC")}}
+        out["topo"] = rows
+    except (OSError, subprocess.SubprocessError, IndexError, ValueError) as e:
+        out["error"] = str(e)
+    return out
 
 
 def host_mem_available() -> int:
