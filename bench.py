@@ -65,7 +65,7 @@ def parse_args():
     ap.add_argument("--push-nccl-share", default="auto",
                     help="with the push exchange, the share (0..1) of every pair's bytes sent by NCCL "
                          "send/recv beside the copy-engine copies; auto = the share measured best for the "
-                         "number of ranks")
+                         "number of ranks on the exchange-bound 70B leg, none on the hash-bound 8B load")
     ap.add_argument("--stage", choices=["mapped", "pinned"], default="pinned",
                     help="host staging of each rank's range: the tmpfs file pages mapped and page-locked in place "
                          "(no second host copy), or a pinned copy read with parallel preads")
@@ -89,16 +89,22 @@ def exchange_mode(args) -> str:
     return "push" if args.exchange == "auto" else args.exchange
 
 
-# Share of every pair's bytes that the push exchange sends over NCCL, by number of ranks.
-# At 2 ranks the copy engines alone already deliver about the peer-copy rate (a 20 % NCCL
-# share measured 48.5 against 47.9 ms of transfer on the 70B TP-2 load).
-AUTO_PUSH_NCCL_SHARE = {2: 0.0}
+# Share of every pair's bytes that the push exchange sends over NCCL, by number of ranks, for
+# loads whose exchange is the long leg (the 70B TP-N load at 2 and 4 ranks). Measured on B200
+# (70B TP-N, device-resident, mean of 3 loads, max over ranks):
+#  * 2 ranks: the copy engines alone already deliver about the peer-copy rate (transfer 47.9 ms;
+#    a 20 / 35 / 50 % NCCL share 48.5 / 49.7 / 54.1 ms);
+#  * 4 ranks: the copy engines reach about 390 GB/s per GPU in the all-to-all (transfer 78.2 ms,
+#    step 83.1 ms); a 30 % share 63.9 ms (step 70.5 ms, now hash-bound), 45 % 65.1, 60 % 70.6.
+# Where the leaf hash is the long leg (the 8B load at every N) the split only takes SM time from
+# the hash (70.3 against 69.0 ms at 4 ranks), so those loads use none.
+AUTO_PUSH_NCCL_SHARE_EXCHANGE_BOUND = {2: 0.0, 4: 0.3}
 
 
-def push_share(args, world: int) -> float:
+def push_share(args, world: int, exchange_bound: bool = False) -> float:
     if args.push_nccl_share != "auto":
         return min(1.0, max(0.0, float(args.push_nccl_share)))
-    return AUTO_PUSH_NCCL_SHARE.get(world, 0.0)
+    return AUTO_PUSH_NCCL_SHARE_EXCHANGE_BOUND.get(world, 0.0) if exchange_bound else 0.0
 
 
 def _size(x: str) -> int:
@@ -1112,7 +1118,7 @@ def c4_leg(args, group, world: int, rank: int, local: int, read_threads: int, ex
                           files=files if from_files else None, read_threads=read_threads,
                           permutes=mine.permutes, view_bytes=mine.view_bytes, expected_root=expected,
                           peer_push=exchange == "push",
-                          push_nccl_share=push_share(args, world) if exchange == "push" else 0.0)
+                          push_nccl_share=push_share(args, world, exchange_bound=True) if exchange == "push" else 0.0)
 
     def mx(x: float) -> float:
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
@@ -1171,7 +1177,7 @@ def c4_leg(args, group, world: int, rank: int, local: int, read_threads: int, ex
                     "stage_read_ms": round(read_ms, 3), "steps": 2, "warmup": 1,
                     "from": "the file in tmpfs, tcx_group_load_files on every rank"},
             "exchange": exchange_summary(exchange, recv, exch_ms, xfer_ms,
-                                         push_share(args, world) if exchange == "push" else 0.0),
+                                         push_share(args, world, exchange_bound=True) if exchange == "push" else 0.0),
             "parity": {"root_matches_cpu_oracle": bool(mn[1].item() > 0), "view_full_ok": bool(mn[0].item() > 0),
                        "view_bytes_checked": int(agg[2].item()), "view_tensors_checked": int(agg[3].item()),
                        "multihash": first["multihash"]},
