@@ -1035,7 +1035,9 @@ def gpu_topology(world: int):
         ids = [ln.split(",")[1].strip() for ln in r.stdout.splitlines() if "," in ln]
         out["pci_bus_ids"] = ids[:world]
         r = subprocess.run(["nvidia-smi", "topo", "-m"], capture_output=True, text=True, timeout=30)
-        lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+        import re
+        text = re.sub(r"\x1b\[[0-9;]*m", "", r.stdout)  # the header is underlined with escape codes
+        lines = [ln for ln in text.splitlines() if ln.strip()]
         head = [h.strip() for h in lines[0].split("\t")] if lines else []
         rows = {}
         for ln in lines[1:]:
