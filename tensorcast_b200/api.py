@@ -91,6 +91,20 @@ def _process_model(world: int, rank: int) -> bool:
         dist.get_rank() == rank
 
 
+def _reader_threads(world: int, rank: int) -> int:
+    """Host reader threads for this rank's file staging: the CPUs this process may run on,
+    shared with the other ranks of this host (the rank threads of this process, or
+    LOCAL_WORLD_SIZE processes), at least 2 and at most 32 per rank."""
+    cpus = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 4)
+    if world <= 1:
+        sharing = 1
+    elif _process_model(world, rank):
+        sharing = max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1") or 1))
+    else:
+        sharing = world  # rank threads of this process
+    return max(2, min(32, cpus // sharing))
+
+
 _GROUPS_LOCK = threading.Lock()
 
 
@@ -237,9 +251,9 @@ class Artifact:
         bounds = stage_bounds(T, L, world)
         lo, hi = bounds[rank], bounds[rank + 1]
         with torch.cuda.device(dev_index):
-            # Buffered reads stream through the group's pinned ring inside the load
-            # (reads, copies and hashing overlap); O_DIRECT reads go through aligned
-            # windows into a pinned copy of the range first.
+            # Buffered reads stream through the group's reader threads and pinned
+            # buffers inside the load (reads, copies and hashing overlap); O_DIRECT
+            # reads go through aligned windows into a pinned copy of the range first.
             h_stage, files = None, canonical_segments(self.index, lo, hi)
             if options and options.direct_io:
                 h_stage = torch.empty(max(hi - lo, 1), dtype=torch.uint8, pin_memory=True)
@@ -260,7 +274,7 @@ class Artifact:
             try:
                 res = group.load(T, L, bounds, rank_jobs, d_stage=d_stage, d_view=d_view, h_stage=h_stage,
                                  files=files, permutes=permutes, view_bytes=view_bytes, expected_root=expected,
-                                 target_ranges=target_ranges)
+                                 target_ranges=target_ranges, read_threads=_reader_threads(world, rank))
             except _native.TcxError as e:
                 code = {15: "DATA_LOSS", 3: "INVALID_ARGUMENT", 4: "DEADLINE_EXCEEDED",
                         5: "NOT_FOUND"}.get(e.code, "INTERNAL")

@@ -118,3 +118,17 @@ def test_canonical_index_multi_file_and_float8(tmp_path):
     assert idx.entries["fp8_e5m2"].dtype == "torch.float8_e5m2"
     assert (idx.entries["fp8_e4m3"].offset, idx.entries["fp8_e4m3"].size) == (0, 8)
     assert (idx.entries["fp8_e5m2"].offset, idx.entries["fp8_e5m2"].size) == (8, 8)
+
+
+def test_reader_threads_shared_by_the_hosts_ranks(monkeypatch):
+    """File staging spreads the host's CPUs over the ranks that stage at once: all of them for
+    one rank, CPUs / LOCAL_WORLD_SIZE for one process per GPU, CPUs / world for rank threads of
+    one process; never fewer than 2 or more than 32 per rank."""
+    monkeypatch.setattr(api.os, "sched_getaffinity", lambda pid: set(range(48)), raising=False)
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "8")
+    assert api._reader_threads(1, 0) == 32
+    monkeypatch.setattr(api, "_process_model", lambda world, rank: True)
+    assert api._reader_threads(8, 3) == 6
+    monkeypatch.setattr(api, "_process_model", lambda world, rank: False)
+    assert api._reader_threads(4, 1) == 12
+    assert api._reader_threads(64, 0) == 2
