@@ -74,6 +74,9 @@ def parse_args():
                          "gather + per-sequence hash, 8 sequence shards dealt to the ranks; disk-hash: "
                          "compute_data_multihash_from_disk_dir of the artifact's directory on one GPU, against "
                          "the reference's single-core CPU path")
+    ap.add_argument("--kv-pages", type=int, default=65536,
+                    help="pool pages of the paged-KV workload (config 5: 65536); smaller pools make the few-GB "
+                         "case used for ncu captures")
     ap.add_argument("--copy-only", metavar="ROWS:COLS:TP",
                     help="only time the view kernels on a bf16 [ROWS, COLS] tensor: the dim-0 and dim-1 "
                          "tensor-parallel shards of rank 0 of TP (copy jobs) and a full transpose")
@@ -797,7 +800,7 @@ def kv_measure(args, world: int, rank: int, local: int):
     from tensorcast_b200 import _native, kvcache
     from oracle import kv as okv
 
-    w = kvcache.workload(seed=3)
+    w = kvcache.workload(seed=3, pool_pages=getattr(args, "kv_pages", 65536))
     shards = [w.shard(8, k, local_pool=True) for k in range(rank, 8, world)]
     pools, runners = [], []
     for k, sh in zip(range(rank, 8, world), shards):
@@ -888,7 +891,7 @@ def kv_measure(args, world: int, rank: int, local: int):
         return None
     return {"value": round(total / ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(ms, 3),
             "steps": args.steps, "warmup": args.warmup,
-            "config": {"workload": "paged KV: 64 planes x 65536 pages [16, 8, 128] bf16, seed 3, "
+            "config": {"workload": f"paged KV: 64 planes x {w.pool_pages} pages [16, 8, 128] bf16, seed 3, "
                                    f"{w.n_seq} sequences (64-4096 tokens), 2 MiB leaves, 8 sequence shards "
                                    "dealt to the ranks",
                        "gathered_bytes": int(total), "sequences": w.n_seq,
