@@ -411,3 +411,25 @@ def test_piece_staged_load_errors_then_recovers(cuda_device, tmp_path, monkeypat
         assert (d_view.cpu().numpy() == canon).all()
     finally:
         g.close()
+
+
+@pytest.mark.parametrize("size,leaf", [(300 << 10, 1 << 20), (6 << 18, 1 << 18)])
+def test_piece_staged_load_edges(cuda_device, tmp_path, monkeypatch, size, leaf):
+    """Piece staging of a range shorter than one leaf (only the short leaf, in pieces) and of
+    a range of whole leaves (no short leaf); root and staged bytes bit-exact."""
+    monkeypatch.setenv("TCX_STAGE", "pieces")
+    monkeypatch.setenv("TCX_STAGE_PIECE", str(1 << 16))
+    canon = np.random.default_rng(size).integers(0, 256, size=size, dtype=np.uint8)
+    segs = _random_segments(tmp_path, canon, np.random.default_rng(size + 1))
+    g = Group(1, 0, 0)
+    try:
+        d_stage = torch.empty(canon.size, dtype=torch.uint8, device="cuda")
+        d_view = torch.zeros(canon.size, dtype=torch.uint8, device="cuda")
+        whole = np.zeros(1, JOB_DTYPE)
+        whole[0] = (0, 0, 0, 0, canon.size, 1)
+        res = g.load(canon.size, leaf, [0, canon.size], [whole], d_stage=d_stage, d_view=d_view, files=segs,
+                     view_bytes=canon.size, read_threads=3)
+        assert res["root"] == oracle.tree_root(oracle.leaf_digests(canon, leaf))
+        assert (d_stage.cpu().numpy() == canon).all() and (d_view.cpu().numpy() == canon).all()
+    finally:
+        g.close()
