@@ -501,7 +501,8 @@ typedef struct tcx_file_stage {
                                        dst_offset relative to bounds[rank]; bytes no segment covers
                                        are zero (the canonical space's alignment pads) */
   uint64_t n_segments;
-  int read_threads;                 /* host reader threads (0: the CPUs the caller may run on, <= 32) */
+  int read_threads;                 /* host reader threads (0: the CPUs the caller may run on, shared among
+                                       the groups alive in this process, 2 to 32) */
   int ring_slots;                   /* slab staging: pinned slabs read ahead (0: 4) */
   uint64_t slot_bytes;              /* slab staging: pinned bytes per slab when plan->slab_bytes is 0
                                        (0: 512 MiB) */

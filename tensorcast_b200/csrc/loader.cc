@@ -55,6 +55,10 @@ namespace {
 using namespace tcx;
 using Clock = std::chrono::steady_clock;
 
+// Groups alive in this process (rank threads of one process each hold one): the
+// default reader count of a load splits the process's CPUs among them.
+std::atomic<int> g_live_groups{0};
+
 constexpr uint64_t kDefaultSlab = 256 * 1024;
 constexpr uint64_t kDefaultWindow = 512ull << 20;  // bytes per peer per exchange round
 constexpr uint64_t kDefaultSlotBytes = 512ull << 20;  // pinned bytes per slab when staging from files
@@ -459,6 +463,7 @@ extern "C" tcx_status tcx_group_create(const uint8_t* unique_id, int world, int 
   if (cudaError_t e = cudaSetDevice(device); e != cudaSuccess)
     return set_errorf(TCX_INTERNAL, "Failed to set CUDA device %d: %s", device, cuda_msg(e).c_str());
   auto* g = new tcx_group();
+  g_live_groups.fetch_add(1);
   g->world = world;
   g->rank = rank;
   g->device = device;
@@ -586,6 +591,7 @@ extern "C" tcx_status tcx_group_destroy(tcx_group* g) {
   for (cudaStream_t s : {g->s_copy, g->s_hash, g->s_comm, g->s_pack, g->s_local})
     if (s) cudaStreamDestroy(s);
   delete g;
+  g_live_groups.fetch_sub(1);
   return TCX_OK;
 }
 
@@ -599,7 +605,11 @@ void ensure_readers(tcx_group* g, int nt) {
   }
 }
 
-int reader_count(const tcx_file_stage& fs) { return fs.read_threads > 0 ? fs.read_threads : std::min(32, affinity_cpus()); }
+// fs.read_threads, or this process's CPUs shared among its live groups (2 to 32).
+int reader_count(const tcx_file_stage& fs) {
+  if (fs.read_threads > 0) return fs.read_threads;
+  return std::max(2, std::min(32, affinity_cpus() / std::max(1, g_live_groups.load())));
+}
 
 template <class Enqueue>
 tcx_status stage_from_files(tcx_group* g, const tcx_file_stage& fs, uint64_t mine, uint64_t L, uint64_t S, uint64_t J,
